@@ -1,0 +1,435 @@
+"""Benchmark of the Qwen3.5 Gated DeltaNet layer on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-prefill]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
+
+Headline (``value``): config 2 of the benchmark spec -- a Qwen3.5-9B-shaped GDN layer (hidden 4096, 16 QK heads,
+32 V heads, dk = dv = 128, conv 4), batch-64 decode, fp32 state ~ N(0, 0.1), as tokens/s of the whole job,
+one decode step per graph replay.  Heads are sharded over N GPUs (one NCCL all-reduce per step): strong
+scaling.  The same line carries config 3 (batch 8 x 8192-token chunked prefill) under ``prefill``, the
+per-stage timing, the roofline of the dominant kernel, the end-to-end number through the public API with
+host buffers, and the CPU baseline (the oracle port on the host cores, rank 0 at N = 1 only).
+
+``--impl reference`` times the reference's CPU path (the oracle restatement of HF Qwen3_5GatedDeltaNet /
+reference.py; the reference's own device code is Tenstorrent-only) on the host cores for the same config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GDN layer tokens/s (decode & 8K prefill), % HBM/tensor roofline, 1-8 B200"
+H, HK, HV, D = 4096, 16, 32, 128          # Qwen3.5-9B GDN geometry
+DECODE_B = 64                              # config 2
+PREFILL_B, PREFILL_T = 8, 8192             # config 3
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of each kernel from the committed ncu summaries (profiles/ncu_traffic.json)."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+# ---------------------------------------------------------------------------------------------------
+# Synthetic layer (the benchmark spec's distributions), generated on the GPU
+# ---------------------------------------------------------------------------------------------------
+def synthetic_weights(seed: int, device, a_max: float = 16.0):
+    from linear_attention_op_b200 import LayerWeights
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    kd, vd = HK * D, HV * D
+    conv_dim = 2 * kd + vd
+    rn = lambda *s: (torch.randn(*s, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return LayerWeights(
+        w_qkv=rn(conv_dim, H), w_z=rn(vd, H), w_a=rn(HV, H), w_b=rn(HV, H),
+        conv_w=((torch.rand(conv_dim, 4, generator=g, device=device) * 2 - 1) * 0.5).bfloat16().float(),
+        a_log=torch.log(1 + torch.rand(HV, generator=g, device=device) * (a_max - 1)),
+        dt_bias=torch.randn(HV, generator=g, device=device) * 0.1,
+        norm_w=0.5 + torch.rand(D, generator=g, device=device),
+        w_out=rn(H, vd), num_k_heads=HK, num_v_heads=HV)
+
+
+def decode_bytes(B: int, world: int = 1) -> dict:
+    """Algorithmic HBM bytes of one decode step (the per-unit figures of the design notes), per GPU."""
+    hv, kd, vd = HV // world, HK * D // world, HV * D // world
+    conv_dim = 2 * kd + vd
+    rows = conv_dim + vd + 2 * hv
+    w_in, w_out = rows * H * 2, H * vd * 2
+    state = 2 * B * hv * D * D * 4
+    conv = 2 * B * conv_dim * 3 * 4
+    act = 2 * B * H * 2
+    proj = B * rows * 4
+    return {
+        "in_proj": w_in + B * H * 2 + conv + proj,
+        "recurrence": state + B * (2 * kd + 2 * vd + 2 * hv) * 4 + B * vd * 2,
+        "out_proj": w_out + B * vd * 2 + B * H * 2,
+        "step": w_in + w_out + state + conv + act,
+    }
+
+
+def prefill_flops(B: int, T: int, world: int = 1) -> dict:
+    n = B * T
+    hv, kd, vd = HV // world, HK * D // world, HV * D // world
+    rows = 2 * kd + 2 * vd + 2 * hv
+    rec = 182955 * n * hv  # per token per head at C = 64, dk = dv = 128
+    return {"in_proj": 2 * n * H * rows, "recurrence": rec, "out_proj": 2 * n * vd * H,
+            "step": 2 * n * H * rows + 2 * n * vd * H + rec}
+
+
+# ---------------------------------------------------------------------------------------------------
+# Clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gdn_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return None
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------------------------------
+def setup_dist(n: int):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def stage_times(layer, run_step, steps: int) -> list[float]:
+    """Average ms per stage over `steps` eager calls, with the library's stage events."""
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(2)]
+    tot = [0.0] * 5
+    for i in range(steps):
+        e = evs[i % 2]
+        layer.set_stage_events(e)
+        run_step()
+        torch.cuda.synchronize()
+        for j in range(5):
+            tot[j] += e[j].elapsed_time(e[j + 1])
+    layer.set_stage_events(None)
+    return [t / steps for t in tot]
+
+
+def run_ours(args):
+    from linear_attention_op_b200 import Qwen35GatedDeltaNet, device_error, launch_count
+    from linear_attention_op_b200.tp import Communicator
+
+    rank, world, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    pk = peaks()
+    traffic = ncu_traffic()
+    comm = Communicator.from_process_group() if world > 1 else None
+    W = synthetic_weights(0, dev)
+    B = DECODE_B
+    layer = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev, tp_rank=rank, tp_size=world, comm=comm,
+                                max_rows=max(B, PREFILL_B * PREFILL_T if args.prefill else B))
+    g = torch.Generator(device=dev).manual_seed(1)
+    s0 = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.1
+    hv0 = rank * (HV // world)
+    layer.set_state(rec_state=s0[:, hv0:hv0 + HV // world])
+    x = torch.randn(B, 1, H, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+
+    # eager warm-up, launch count per step
+    n0 = launch_count()
+    with torch.cuda.stream(stream):
+        layer.forward_into(x, out, stream=stream)
+    torch.cuda.synchronize()
+    launches_per_step = launch_count() - n0
+    if device_error() != 0:
+        raise SystemExit("device error during warm-up")
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        layer.forward_into(x, out, stream=stream)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    ms_step = ms / args.steps
+    value = B * args.steps / (ms / 1e3)
+
+    # per-stage timing (eager, same step), roofline of the dominant kernel
+    def dec_step():
+        layer.forward_into(x, out, stream=torch.cuda.current_stream())
+
+    st = stage_times(layer, dec_step, min(args.steps, 50))
+    names = ["in_proj", "conv", "recurrence", "out_proj", "allreduce"]
+    byt = decode_bytes(B, world)
+    dec_stage = {n: round(t * 1e3, 2) for n, t in zip(names, st) if n != "conv"}
+    dom = max(["in_proj", "recurrence", "out_proj"], key=lambda n: dec_stage[n])
+    achieved = byt[dom] / (dec_stage[dom] * 1e-6) / 1e9
+    tr = traffic.get(f"decode_{dom}")
+    roofline = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "traffic": tr, "algorithmic_bytes": byt[dom], "peak_source": pk["source"]}
+    step_achieved = byt["step"] / (ms_step * 1e-3) / 1e9
+    decode_detail = {"stage_us": dec_stage, "step_bytes": byt["step"], "step_gbs": round(step_achieved, 1),
+                     "step_hbm_frac": round(step_achieved / pk["hbm_gbs"], 4)}
+
+    # end to end through the public API, host buffers (pinned), H2D + D2H inside the timed region
+    xh = x.detach().cpu().pin_memory()
+    for _ in range(3):
+        layer(xh)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_steps = min(args.steps, 100)
+    t0 = time.perf_counter()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for _ in range(e2e_steps):
+        yh = layer(xh)
+    ee.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(max(es.elapsed_time(ee), (time.perf_counter() - t0) * 1e3), world)
+    e2e = {"value": round(B * e2e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": yh.numel() * yh.element_size(),
+           "steps": e2e_steps, "path": "Qwen35GatedDeltaNet.__call__ (C-ABI gdn_layer_forward)"}
+
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 (fp32 state, fp32 accumulation)", "data": "synthetic",
+        "config": {"workload": "cfg2: Qwen3.5-9B GDN layer decode, batch 64, fp32 state ~N(0,0.1)",
+                   "model": "Qwen3.5-9B GDN layer (random init)", "global_batch": B, "seq_len": 1,
+                   "parallelism": f"tp{world} head-parallel" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: 417 MB of weights + state per step > 126 MB",
+                   "graph": "one decode step per CUDA-graph replay"},
+        "roofline": roofline, "decode": decode_detail, "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step,
+        "clocks": clk.summary(),
+    }
+    if args.prefill:
+        result["prefill"] = run_prefill(args, layer, dev, world, pk, traffic)
+    if device_error() != 0:
+        raise SystemExit("device error during the benchmark")
+    if rank == 0 and world == 1 and not args.no_cpu:
+        result["cpu_baseline"] = cpu_baseline()
+    del graph
+    if comm is not None:
+        comm.close()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_prefill(args, layer_dec, dev, world, pk, traffic):
+    """Config 3: batch 8 x 8192-token chunked prefill (weights shared with the decode layer)."""
+    B, T = PREFILL_B, PREFILL_T
+    layer_p = layer_dec.with_batch(B)  # same device weights, own batch and state
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(B, T, H, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    steps = max(1, min(args.steps, args.prefill_steps))
+    for _ in range(2):
+        layer_p.forward_into(x, out)
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        s.record()
+        for _ in range(steps):
+            layer_p.forward_into(x, out)
+        e.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e), world) / steps
+    st = stage_times(layer_p, lambda: layer_p.forward_into(x, out), min(steps, 3))
+    names = ["in_proj", "conv", "recurrence", "out_proj", "allreduce"]
+    stage = {n: round(t, 3) for n, t in zip(names, st)}
+    fl = prefill_flops(B, T, world)
+    tf = lambda n: fl[n] / (stage[n] * 1e-3) / 1e12
+    return {
+        "workload": "cfg3: Qwen3.5-9B GDN layer chunked prefill, batch 8 x 8192 tokens, chunk 64",
+        "value": round(B * T / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3), "steps": steps,
+        "stage_ms": stage,
+        "roofline": {"kernel": "in_proj", "bound": "tensor", "achieved": round(tf("in_proj"), 1),
+                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(tf("in_proj") / pk["bf16_tflops_sustained"], 4),
+                     "traffic": traffic.get("prefill_in_proj"), "peak_source": pk["source"] + " (sustained)"},
+        "step_tflops": round(fl["step"] / (ms * 1e-3) / 1e12, 1),
+        "step_tensor_frac": round(fl["step"] / (ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
+        "recurrence_tflops": round(tf("recurrence"), 2),
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port on the host cores
+# ---------------------------------------------------------------------------------------------------
+def cpu_decode_rate(budget_s: float = 15.0, max_steps: int | None = None, warmup: int = 1):
+    from oracle import gdn_oracle as O  # the CPU restatement of the reference path
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = O.make_weights(H, HK, HV, seed=0)
+    B = DECODE_B
+    x = O.make_hidden(B, 1, H, seed=1)
+    s = torch.randn(B, HV, D, D, generator=torch.Generator().manual_seed(1)) * 0.1
+    c = torch.zeros(B, 3, 2 * HK * D + HV * D)
+    with torch.no_grad():
+        for _ in range(warmup):
+            O.layer_forward(w, x, s, c)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            _, s, c = O.layer_forward(w, x, s, c)
+            n += 1
+            el = time.perf_counter() - t0
+            if (max_steps is not None and n >= max_steps) or (max_steps is None and el >= budget_s):
+                break
+    return B * n / el, n, el, torch.get_num_threads()
+
+
+def cpu_baseline():
+    rate, n, el, cores = cpu_decode_rate()
+    return {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} cfg2 decode steps (batch 64, 9B GDN layer, fp32) in {el:.1f} s on the host cores"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    rate_w = cpu_decode_rate(max_steps=args.warmup, warmup=0) if args.warmup > 0 else None
+    del rate_w
+    rate, n, el, cores = cpu_decode_rate(max_steps=args.steps, warmup=0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(rate, 1), "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": n, "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "cfg2: Qwen3.5-9B GDN layer decode, batch 64, fp32 state ~N(0,0.1)",
+                   "model": "Qwen3.5-9B GDN layer (random init)", "global_batch": DECODE_B, "seq_len": 1,
+                   "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} full cfg2 decode steps on the host cores (the reference's device code "
+                                   f"is Tenstorrent-only; this is its CPU golden path restated)"},
+        "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false")
+    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,163 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) Qwen3.5 Gated DeltaNet layer.
+ *
+ * The ABI keeps the per-layer op API of the reference (chz05/linear_attention_op): weights in; hidden
+ * states plus the recurrent and conv state in and out.  It is plain C: opaque handles, plain pointers and
+ * sizes, status codes, no exceptions across the boundary, no torch types.  All tensor pointers passed to
+ * the compute entry points are CUDA device pointers; `stream` is a cudaStream_t (NULL = legacy stream);
+ * work is stream-ordered and asynchronous.  Handles are thread-compatible: use one handle per stream.
+ *
+ * Layouts (row-major, "rows" are sequence-major tokens b*T + t, as in the reference
+ * wormhole_n150/qwen3.5_9B/kernels/layer_reader.cpp:108-110):
+ *   x, out      bf16 [B, T, hidden]
+ *   rec_state   fp32 [B, Hv_local, 128, 128], S[k_index][v_index]      (9B/reference.py:26-34)
+ *   conv_state  fp32 [B, 3, conv_dim_local], row j = pre-conv input at time T-3+j
+ *               (the reference's 3-row history, 9B/kernels/layer_reader.cpp:184-197)
+ *   conv_dim_local = 2 * Hk_local * 128 + Hv_local * 128, channel order [q | k | v] of this rank's heads.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+typedef enum gdn_status {
+  GDN_OK = 0,
+  GDN_ERR_INVALID_ARGUMENT = 1, /* bad size, shape or alignment */
+  GDN_ERR_NULL_POINTER = 2,
+  GDN_ERR_UNSUPPORTED = 3,      /* geometry this build does not implement (e.g. head dim != 128) */
+  GDN_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+  GDN_ERR_NCCL = 5,             /* NCCL missing or a NCCL call failed */
+  GDN_ERR_TIMEOUT = 6,          /* a kernel's bounded wait expired (see gdn_device_error) */
+  GDN_ERR_OUT_OF_MEMORY = 7
+} gdn_status;
+
+/* Layer geometry (global, before head sharding).  Mirrors the HF Qwen3_5TextConfig fields the
+ * reference reads (0.8B/test_gdn_l1.py:11-14) and the asserts of 9B/gdn_layer.py:61-64. */
+typedef struct gdn_dims {
+  int32_t hidden;      /* hidden size; multiple of 64 */
+  int32_t num_k_heads; /* Hk */
+  int32_t num_v_heads; /* Hv, a multiple of Hk (GQA: v-head h reads k-head h / (Hv/Hk)) */
+  int32_t head_k_dim;  /* must be 128 */
+  int32_t head_v_dim;  /* must be 128 */
+  int32_t conv_kernel; /* must be 4 */
+  float eps;           /* RMSNorm epsilon (1e-6) */
+  int32_t chunk;       /* prefill chunk; 0 or 64 */
+} gdn_dims;
+
+/* One layer's weights in Hugging Face Qwen3_5GatedDeltaNet layout (global, unsharded).  Pointers may be
+ * host or device memory; gdn_layer_create copies this rank's head shard into layer-owned device buffers
+ * (the reference copies and re-lays out the HF weights in its constructor, 9B/gdn_layer.py:90-127). */
+typedef struct gdn_weights {
+  const uint16_t* w_qkv;  /* bf16 [2*Hk*128 + Hv*128, hidden]  in_proj_qkv.weight */
+  const uint16_t* w_z;    /* bf16 [Hv*128, hidden]             in_proj_z.weight   */
+  const uint16_t* w_a;    /* bf16 [Hv, hidden]                 in_proj_a.weight   */
+  const uint16_t* w_b;    /* bf16 [Hv, hidden]                 in_proj_b.weight   */
+  const float* conv_w;    /* fp32 [2*Hk*128 + Hv*128, 4]       conv1d.weight[:, 0, :] */
+  const float* a_log;     /* fp32 [Hv]                         A_log              */
+  const float* dt_bias;   /* fp32 [Hv]                         dt_bias            */
+  const float* norm_w;    /* fp32 [128]                        norm.weight        */
+  const uint16_t* w_out;  /* bf16 [hidden, Hv*128]             out_proj.weight    */
+} gdn_weights;
+
+/* Sizes of this rank's shard, for allocating the state buffers. */
+typedef struct gdn_layer_info {
+  int32_t hidden;
+  int32_t num_k_heads_local;
+  int32_t num_v_heads_local;
+  int32_t conv_dim_local;
+  int32_t tp_rank;
+  int32_t tp_size;
+  int64_t rec_state_floats_per_seq;  /* Hv_local * 128 * 128 */
+  int64_t conv_state_floats_per_seq; /* 3 * conv_dim_local */
+  int64_t workspace_bytes;           /* currently reserved workspace */
+} gdn_layer_info;
+
+typedef struct gdn_layer gdn_layer; /* opaque */
+typedef struct gdn_comm gdn_comm;   /* opaque: a NCCL communicator over the tensor-parallel group */
+
+/* Build a layer handle for tensor-parallel rank `tp_rank` of `tp_size` (1 = single GPU), on the current
+ * CUDA device.  Rank r owns k-heads [r*Hk/G, (r+1)*Hk/G) and v-heads [r*Hv/G, (r+1)*Hv/G): in_proj rows
+ * of those heads, out_proj columns of those v-heads.  Replaces Qwen35GatedDeltaNetTT.__init__
+ * (9B/gdn_layer.py:55-78) and Qwen35_08B_GDNStackL1's per-layer _Layer (0.8B/gdn_l1.py:91-130). */
+GDN_API gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* weights, int32_t tp_rank, int32_t tp_size,
+                            gdn_layer** out_layer);
+
+GDN_API gdn_status gdn_layer_destroy(gdn_layer* layer);
+
+GDN_API gdn_status gdn_layer_get_info(const gdn_layer* layer, gdn_layer_info* info);
+
+/* Pre-allocate the workspace for calls of up to `max_tokens` = B*T rows, so that later forwards
+ * allocate nothing (required before capturing forwards into a CUDA graph). */
+GDN_API gdn_status gdn_layer_reserve(gdn_layer* layer, int64_t max_tokens);
+
+/* One layer call that continues from (rec_state, conv_state) and updates both in place:
+ *   T == 1  decode step (one token per sequence);  T > 1  chunked prefill of T tokens per sequence.
+ * out receives the layer output (bf16 [B, T, hidden]); with tp_size > 1 every rank receives the full,
+ * all-reduced output (one NCCL all-reduce per call over `comm`).  With comm == NULL the call skips the
+ * all-reduce and out holds this rank's partial sum (for callers that reduce themselves).
+ * Replaces Qwen35GatedDeltaNetTT.__call__ / _forward_rows (9B/gdn_layer.py:244-292) and
+ * Qwen35_08B_GDNStackL1.forward_device (0.8B/gdn_l1.py:295-307).  x may alias nothing else. */
+GDN_API gdn_status gdn_layer_forward(gdn_layer* layer, const uint16_t* x, int32_t batch, int32_t seq_len, float* rec_state,
+                             float* conv_state, uint16_t* out, gdn_comm* comm, void* stream);
+
+/* Optional stage timing: each forward records events[i] (cudaEvent_t, created by the caller) on its stream:
+ * 0 start, 1 after in_proj, 2 after the prefill conv (= 1 for decode), 3 after the recurrence (decode
+ * kernel or chunked prefill), 4 after out_proj, 5 after the all-reduce.  count 0 disables.  The reference
+ * measures the same per-op split with its device profiler (9B/README.md:137-145). */
+GDN_API gdn_status gdn_layer_set_stage_events(gdn_layer* layer, void* const* events, int32_t count);
+
+/* Recurrence only (no projections, conv or norm), token by token, state updated in place:
+ *   q, k fp32 [B, T, Hk, 128]; v fp32 [B, T, Hv, 128]; g (log decay), beta fp32 [B, T, Hv];
+ *   state fp32 [B, Hv, 128, 128]; o fp32 [B, T, Hv, 128].
+ * scale <= 0 means 128^-0.5.  Replaces GatedDeltaRuleL1.__call__ / forward_packed
+ * (9B/gated_delta_l1.py:247-272) with the math of 9B/reference.py:11-35. */
+GDN_API gdn_status gdn_recurrence_forward(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                                  int32_t batch, int32_t seq_len, int32_t num_k_heads, int32_t num_v_heads,
+                                  int32_t use_qk_l2norm, float scale, float* state, float* o, void* stream);
+
+/* The tcgen05 GEMM building block of the layer's projections: C = A * B^T with A bf16 [m, k] (row stride
+ * lda) and B bf16 [n, k] (row stride ldb), fp32 accumulation.  out_kind: 0 = fp32 C[m][n], 1 = bf16 C[m][n],
+ * 2 = fp32 C[n][m] (transposed), 3 = bf16 C[n][m]; ldo is the output row stride.  ksplit 0 = automatic,
+ * 1..8 = K split over a thread-block cluster.  The reference's projections are ttnn.linear calls
+ * (9B/gdn_layer.py:255-259,272-276). */
+GDN_API gdn_status gdn_gemm_bf16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int32_t m, int32_t n,
+                                 int32_t k, int32_t out_kind, void* out, int64_t ldo, int32_t ksplit, void* stream);
+
+/* Tensor-parallel communicator (NCCL, loaded at run time).  Rank 0 calls gdn_comm_get_unique_id and
+ * shares the 128 bytes with the other ranks out of band; every rank then calls gdn_comm_create with its
+ * own CUDA device current. */
+GDN_API gdn_status gdn_comm_get_unique_id(void* id_out, size_t id_bytes);
+GDN_API gdn_status gdn_comm_create(const void* id, size_t id_bytes, int32_t rank, int32_t world, gdn_comm** out_comm);
+GDN_API gdn_status gdn_comm_destroy(gdn_comm* comm);
+
+/* Synchronises the current device and returns (and clears) the device error word that bounded waits
+ * inside the kernels set; 0 = no error. */
+GDN_API gdn_status gdn_device_error(int32_t* code_out);
+
+/* Human-readable description of the last error on the calling thread ("" if none). */
+GDN_API const char* gdn_last_error_string(void);
+
+/* Number of CUDA kernels this library has launched since it was loaded. */
+GDN_API uint64_t gdn_kernel_launch_count(void);
+
+/* ABI version (GDN_ABI_VERSION) of the loaded library. */
+GDN_API int32_t gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

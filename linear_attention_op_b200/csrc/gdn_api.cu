@@ -1,0 +1,469 @@
+// C-ABI implementation: layer handles (head-sharded weight copies, workspace), the decode and prefill
+// pipelines, the recurrence-only op, and the NCCL communicator (loaded with dlopen so the library has no
+// link-time NCCL dependency).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "../../include/gdn_b200.h"
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+using namespace gdn;
+
+// ------------------------------------------------------------------------------------------------
+// Errors
+// ------------------------------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+
+static gdn_status fail(gdn_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return st;
+}
+
+#define GDN_CUDA(call)                                                                                   \
+  do {                                                                                                   \
+    cudaError_t _e = (call);                                                                             \
+    if (_e != cudaSuccess) {                                                                             \
+      if (_e == cudaErrorMemoryAllocation)                                                               \
+        return fail(GDN_ERR_OUT_OF_MEMORY, "%s: %s (%s:%d)", #call, cudaGetErrorString(_e), __FILE__,    \
+                    __LINE__);                                                                           \
+      return fail(GDN_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(_e), __FILE__, __LINE__);   \
+    }                                                                                                    \
+  } while (0)
+
+// ------------------------------------------------------------------------------------------------
+// NCCL (dlopen)
+// ------------------------------------------------------------------------------------------------
+struct NcclApi {
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char* (*getErrorString)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+static const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the copy torch already loaded, if any
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.getUniqueId = reinterpret_cast<decltype(api.getUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    api.commInitRank = reinterpret_cast<decltype(api.commInitRank)>(dlsym(h, "ncclCommInitRank"));
+    api.commDestroy = reinterpret_cast<decltype(api.commDestroy)>(dlsym(h, "ncclCommDestroy"));
+    api.allReduce = reinterpret_cast<decltype(api.allReduce)>(dlsym(h, "ncclAllReduce"));
+    api.getErrorString = reinterpret_cast<decltype(api.getErrorString)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.allReduce && api.getErrorString;
+  });
+  return api;
+}
+
+struct gdn_comm {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+};
+
+// ------------------------------------------------------------------------------------------------
+// Layer
+// ------------------------------------------------------------------------------------------------
+struct gdn_layer {
+  gdn_dims dims{};
+  int tp_rank = 0, tp_size = 1;
+  int device = 0;
+  int hk = 0, hv = 0;              // local heads
+  int kd = 0, vd = 0, conv_dim = 0; // local channel counts
+  int rows = 0;                     // fused in_proj rows: conv_dim + vd + 2 hv
+  int proj_ld = 0;                  // row stride of the in_proj output buffer: rows rounded up to 8
+  __nv_bfloat16* w_in = nullptr;    // [rows, hidden]: [q | k | v | z | a | b]
+  __nv_bfloat16* w_out = nullptr;   // [hidden, vd]
+  float* conv_w = nullptr;          // [conv_dim, 4]
+  float* a_log = nullptr;           // [hv]
+  float* dt_bias = nullptr;         // [hv]
+  float* norm_w = nullptr;          // [128]
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  cudaEvent_t stage_events[6] = {};  // optional stage timing (gdn_layer_set_stage_events)
+  int n_stage_events = 0;
+};
+
+static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// Workspace layout for n token rows: proj fp32 [n, proj_ld] | qkv fp32 [n, conv_dim] | y bf16 [n, vd]
+static size_t workspace_bytes(const gdn_layer* L, int64_t n) {
+  return align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4) + align256(n * L->vd * 2);
+}
+
+static gdn_status ensure_workspace(gdn_layer* L, int64_t n, cudaStream_t stream) {
+  const size_t need = workspace_bytes(L, n);
+  if (need <= L->ws_bytes) return GDN_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+    return fail(GDN_ERR_INVALID_ARGUMENT,
+                "workspace for %lld rows is not reserved; call gdn_layer_reserve before stream capture",
+                static_cast<long long>(n));
+  if (L->ws) GDN_CUDA(cudaFree(L->ws));
+  L->ws = nullptr;
+  L->ws_bytes = 0;
+  GDN_CUDA(cudaMalloc(&L->ws, need));
+  L->ws_bytes = need;
+  return GDN_OK;
+}
+
+static void free_layer(gdn_layer* L) {
+  if (!L) return;
+  for (void* p : {static_cast<void*>(L->w_in), static_cast<void*>(L->w_out), static_cast<void*>(L->conv_w),
+                  static_cast<void*>(L->a_log), static_cast<void*>(L->dt_bias), static_cast<void*>(L->norm_w),
+                  L->ws})
+    if (p) cudaFree(p);
+  delete L;
+}
+
+// Copy `nrows` rows of `cols` elements (elem bytes each) from a (host or device) matrix with row stride
+// src_ld into a dense destination.
+static cudaError_t copy_rows(void* dst, const void* src, int64_t src_ld, int64_t row0, int64_t nrows, int64_t cols,
+                             size_t elem) {
+  return cudaMemcpy2D(dst, cols * elem, static_cast<const char*>(src) + row0 * src_ld * elem, src_ld * elem,
+                      cols * elem, nrows, cudaMemcpyDefault);
+}
+
+extern "C" gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* w, int32_t tp_rank, int32_t tp_size,
+                                       gdn_layer** out_layer) {
+  if (!dims || !w || !out_layer) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_create: null argument");
+  *out_layer = nullptr;
+  const gdn_dims d = *dims;
+  if (!w->w_qkv || !w->w_z || !w->w_a || !w->w_b || !w->conv_w || !w->a_log || !w->dt_bias || !w->norm_w ||
+      !w->w_out)
+    return fail(GDN_ERR_NULL_POINTER, "gdn_layer_create: a weight pointer is null");
+  if (d.head_k_dim != kHeadDim || d.head_v_dim != kHeadDim)
+    return fail(GDN_ERR_UNSUPPORTED, "head dims %d/%d unsupported (only 128)", d.head_k_dim, d.head_v_dim);
+  if (d.conv_kernel != 4) return fail(GDN_ERR_UNSUPPORTED, "conv kernel %d unsupported (only 4)", d.conv_kernel);
+  if (d.chunk != 0 && d.chunk != 64) return fail(GDN_ERR_UNSUPPORTED, "chunk %d unsupported (only 64)", d.chunk);
+  if (d.hidden <= 0 || d.hidden % 64)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "hidden %d must be a positive multiple of 64", d.hidden);
+  if (d.num_k_heads <= 0 || d.num_v_heads <= 0 || d.num_v_heads % d.num_k_heads)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "num_v_heads %d must be a multiple of num_k_heads %d", d.num_v_heads,
+                d.num_k_heads);
+  if (!(d.eps > 0.f)) return fail(GDN_ERR_INVALID_ARGUMENT, "eps must be > 0");
+  if (tp_size <= 0 || tp_rank < 0 || tp_rank >= tp_size)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "tp_rank %d / tp_size %d", tp_rank, tp_size);
+  if (d.num_k_heads % tp_size || d.num_v_heads % tp_size)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "tp_size %d must divide num_k_heads %d and num_v_heads %d", tp_size,
+                d.num_k_heads, d.num_v_heads);
+
+  gdn_layer* L = new (std::nothrow) gdn_layer();
+  if (!L) return fail(GDN_ERR_OUT_OF_MEMORY, "host allocation failed");
+  L->dims = d;
+  L->tp_rank = tp_rank;
+  L->tp_size = tp_size;
+  cudaGetDevice(&L->device);
+  L->hk = d.num_k_heads / tp_size;
+  L->hv = d.num_v_heads / tp_size;
+  L->kd = L->hk * kHeadDim;
+  L->vd = L->hv * kHeadDim;
+  L->conv_dim = 2 * L->kd + L->vd;
+  L->rows = L->conv_dim + L->vd + 2 * L->hv;
+  L->proj_ld = (L->rows + 7) & ~7;
+  const int64_t h = d.hidden;
+  const int64_t kd_g = static_cast<int64_t>(d.num_k_heads) * kHeadDim;
+  const int64_t k0 = static_cast<int64_t>(tp_rank) * L->kd;  // first local q/k channel (global index)
+  const int64_t v0 = static_cast<int64_t>(tp_rank) * L->vd;  // first local v/z channel
+  const int64_t hv0 = static_cast<int64_t>(tp_rank) * L->hv; // first local v-head
+
+  auto run = [&]() -> gdn_status {
+    GDN_CUDA(cudaMalloc(&L->w_in, static_cast<size_t>(L->rows) * h * 2));
+    GDN_CUDA(cudaMalloc(&L->w_out, static_cast<size_t>(h) * L->vd * 2));
+    GDN_CUDA(cudaMalloc(&L->conv_w, static_cast<size_t>(L->conv_dim) * 4 * 4));
+    GDN_CUDA(cudaMalloc(&L->a_log, L->hv * 4));
+    GDN_CUDA(cudaMalloc(&L->dt_bias, L->hv * 4));
+    GDN_CUDA(cudaMalloc(&L->norm_w, kHeadDim * 4));
+    char* win = reinterpret_cast<char*>(L->w_in);
+    int64_t r = 0;
+    // q, k, v rows of in_proj_qkv, then z, a, b
+    GDN_CUDA(copy_rows(win + r * h * 2, w->w_qkv, h, k0, L->kd, h, 2)); r += L->kd;
+    GDN_CUDA(copy_rows(win + r * h * 2, w->w_qkv, h, kd_g + k0, L->kd, h, 2)); r += L->kd;
+    GDN_CUDA(copy_rows(win + r * h * 2, w->w_qkv, h, 2 * kd_g + v0, L->vd, h, 2)); r += L->vd;
+    GDN_CUDA(copy_rows(win + r * h * 2, w->w_z, h, v0, L->vd, h, 2)); r += L->vd;
+    GDN_CUDA(copy_rows(win + r * h * 2, w->w_a, h, hv0, L->hv, h, 2)); r += L->hv;
+    GDN_CUDA(copy_rows(win + r * h * 2, w->w_b, h, hv0, L->hv, h, 2)); r += L->hv;
+    // conv taps of the same channels
+    char* cw = reinterpret_cast<char*>(L->conv_w);
+    GDN_CUDA(copy_rows(cw, w->conv_w, 4, k0, L->kd, 4, 4));
+    GDN_CUDA(copy_rows(cw + static_cast<int64_t>(L->kd) * 16, w->conv_w, 4, kd_g + k0, L->kd, 4, 4));
+    GDN_CUDA(copy_rows(cw + static_cast<int64_t>(2 * L->kd) * 16, w->conv_w, 4, 2 * kd_g + v0, L->vd, 4, 4));
+    GDN_CUDA(cudaMemcpy(L->a_log, w->a_log + hv0, L->hv * 4, cudaMemcpyDefault));
+    GDN_CUDA(cudaMemcpy(L->dt_bias, w->dt_bias + hv0, L->hv * 4, cudaMemcpyDefault));
+    GDN_CUDA(cudaMemcpy(L->norm_w, w->norm_w, kHeadDim * 4, cudaMemcpyDefault));
+    // out_proj columns of the local v-heads: [hidden, vd] slice of [hidden, Hv*128]
+    const int64_t vd_g = static_cast<int64_t>(d.num_v_heads) * kHeadDim;
+    GDN_CUDA(cudaMemcpy2D(L->w_out, L->vd * 2, reinterpret_cast<const char*>(w->w_out) + v0 * 2, vd_g * 2,
+                          L->vd * 2, h, cudaMemcpyDefault));
+    GDN_CUDA(cudaDeviceSynchronize());
+    return GDN_OK;
+  };
+  const gdn_status st = run();
+  if (st != GDN_OK) {
+    free_layer(L);
+    return st;
+  }
+  *out_layer = L;
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_layer_destroy(gdn_layer* layer) {
+  if (!layer) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_destroy: null layer");
+  free_layer(layer);
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_layer_get_info(const gdn_layer* L, gdn_layer_info* info) {
+  if (!L || !info) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_get_info: null argument");
+  info->hidden = L->dims.hidden;
+  info->num_k_heads_local = L->hk;
+  info->num_v_heads_local = L->hv;
+  info->conv_dim_local = L->conv_dim;
+  info->tp_rank = L->tp_rank;
+  info->tp_size = L->tp_size;
+  info->rec_state_floats_per_seq = static_cast<int64_t>(L->hv) * kHeadDim * kHeadDim;
+  info->conv_state_floats_per_seq = 3LL * L->conv_dim;
+  info->workspace_bytes = static_cast<int64_t>(L->ws_bytes);
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_layer_reserve(gdn_layer* L, int64_t max_tokens) {
+  if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_reserve: null layer");
+  if (max_tokens <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens must be > 0");
+  return ensure_workspace(L, max_tokens, nullptr);
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static cudaError_t stage_mark(const gdn_layer* L, int i, cudaStream_t s) {
+  return i < L->n_stage_events && L->stage_events[i] ? cudaEventRecord(L->stage_events[i], s) : cudaSuccess;
+}
+
+extern "C" gdn_status gdn_layer_set_stage_events(gdn_layer* L, void* const* events, int32_t count) {
+  if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_set_stage_events: null layer");
+  if (count < 0 || count > 6 || (count > 0 && !events))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_layer_set_stage_events: count %d", count);
+  for (int i = 0; i < 6; ++i) L->stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  L->n_stage_events = count;
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t B, int32_t T, float* rec_state,
+                                        float* conv_state, uint16_t* out, gdn_comm* comm, void* stream_ptr) {
+  if (!L || !x || !rec_state || !conv_state || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_forward: null argument");
+  if (B <= 0 || T <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch %d and seq_len %d must be > 0", B, T);
+  if (!aligned16(x) || !aligned16(out) || !aligned16(rec_state) || !aligned16(conv_state))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  if (L->tp_size > 1 && comm) {
+    if (comm->world != L->tp_size || comm->rank != L->tp_rank)
+      return fail(GDN_ERR_INVALID_ARGUMENT, "communicator rank %d/%d does not match layer rank %d/%d", comm->rank,
+                  comm->world, L->tp_rank, L->tp_size);
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int64_t n = static_cast<int64_t>(B) * T;
+  gdn_status st = ensure_workspace(L, n, stream);
+  if (st != GDN_OK) return st;
+  const int h = L->dims.hidden;
+  char* ws = static_cast<char*>(L->ws);
+  float* proj = reinterpret_cast<float*>(ws);
+  float* qkv = reinterpret_cast<float*>(ws + align256(n * L->proj_ld * 4));
+  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4));
+  const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
+
+  GDN_CUDA(stage_mark(L, 0, stream));
+  if (T == 1) {
+    // ---- decode: in_proj (weights as the 128-row operand) with conv + gating fused into the epilogue
+    GemmEpiArgs ep;
+    ep.out = proj;
+    ep.ld = L->proj_ld;
+    ep.conv_rows = L->conv_dim;
+    ep.z_rows = L->vd;
+    ep.nheads = L->hv;
+    ep.conv_w = L->conv_w;
+    ep.conv_state = conv_state;
+    ep.a_log = L->a_log;
+    ep.dt_bias = L->dt_bias;
+    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream));
+    GDN_CUDA(stage_mark(L, 1, stream));
+    GDN_CUDA(stage_mark(L, 2, stream));
+    RecurrenceArgs ra;
+    ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
+    ra.k = proj + L->kd; ra.k_tok = L->proj_ld; ra.k_head = kHeadDim;
+    ra.v = proj + 2 * L->kd; ra.v_tok = L->proj_ld; ra.v_head = kHeadDim;
+    ra.z = proj + z_off; ra.z_tok = L->proj_ld; ra.z_head = kHeadDim;
+    ra.g = proj + a_off; ra.g_tok = L->proj_ld; ra.g_head = 1;
+    ra.beta = proj + b_off; ra.b_tok = L->proj_ld; ra.b_head = 1;
+    ra.norm_w = L->norm_w;
+    ra.eps = L->dims.eps;
+    ra.y = y; ra.y_tok = L->vd; ra.y_head = kHeadDim;
+    ra.state = rec_state;
+    ra.B = B; ra.T = 1; ra.Hk = L->hk; ra.Hv = L->hv;
+    ra.scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
+    ra.l2norm = 1;
+    GDN_CUDA(recurrence_forward(ra, stream));
+    GDN_CUDA(stage_mark(L, 3, stream));
+    GemmEpiArgs eo;
+    eo.out = out;
+    eo.ld = h;
+    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream));
+    GDN_CUDA(stage_mark(L, 4, stream));
+  } else {
+    // ---- prefill: in_proj -> conv -> chunked recurrence + gated RMSNorm -> out_proj
+    GemmEpiArgs ep;
+    ep.out = proj;
+    ep.ld = L->proj_ld;
+    GDN_CUDA(gemm_bf16_tn(x, h, L->w_in, h, static_cast<int>(n), L->rows, h, kEpiStoreF32, ep, 1, stream));
+    GDN_CUDA(stage_mark(L, 1, stream));
+    GDN_CUDA(conv_prefill(proj, L->proj_ld, qkv, L->conv_dim, L->conv_w, conv_state, B, T, L->conv_dim, stream));
+    GDN_CUDA(stage_mark(L, 2, stream));
+    ChunkArgs ca;
+    ca.qkv = qkv; ca.qkv_ld = L->conv_dim;
+    ca.proj = proj; ca.proj_ld = L->proj_ld;
+    ca.z_off = z_off; ca.a_off = a_off; ca.b_off = b_off;
+    ca.a_log = L->a_log; ca.dt_bias = L->dt_bias; ca.norm_w = L->norm_w; ca.eps = L->dims.eps;
+    ca.state = rec_state; ca.y = y;
+    ca.B = B; ca.T = T; ca.Hk = L->hk; ca.Hv = L->hv;
+    GDN_CUDA(chunk_prefill(ca, stream));
+    GDN_CUDA(stage_mark(L, 3, stream));
+    GemmEpiArgs eo;
+    eo.out = out;
+    eo.ld = h;
+    GDN_CUDA(gemm_bf16_tn(y, L->vd, L->w_out, L->vd, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, 1, stream));
+    GDN_CUDA(stage_mark(L, 4, stream));
+  }
+  if (L->tp_size > 1 && comm) {
+    const NcclApi& api = nccl();
+    if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
+    ncclResult_t r = api.allReduce(out, out, static_cast<size_t>(n) * h, ncclBfloat16, ncclSum, comm->comm, stream);
+    if (r != ncclSuccess) return fail(GDN_ERR_NCCL, "ncclAllReduce: %s", api.getErrorString(r));
+  }
+  GDN_CUDA(stage_mark(L, 5, stream));
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_recurrence_forward(const float* q, const float* k, const float* v, const float* g,
+                                             const float* beta, int32_t B, int32_t T, int32_t Hk, int32_t Hv,
+                                             int32_t use_qk_l2norm, float scale, float* state, float* o,
+                                             void* stream) {
+  if (!q || !k || !v || !g || !beta || !state || !o) return fail(GDN_ERR_NULL_POINTER, "gdn_recurrence_forward: null argument");
+  if (B <= 0 || T <= 0 || Hk <= 0 || Hv <= 0 || Hv % Hk)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "bad shape B=%d T=%d Hk=%d Hv=%d", B, T, Hk, Hv);
+  if (!aligned16(state)) return fail(GDN_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+  RecurrenceArgs ra;
+  ra.q = q; ra.q_tok = static_cast<int64_t>(Hk) * kHeadDim; ra.q_head = kHeadDim;
+  ra.k = k; ra.k_tok = static_cast<int64_t>(Hk) * kHeadDim; ra.k_head = kHeadDim;
+  ra.v = v; ra.v_tok = static_cast<int64_t>(Hv) * kHeadDim; ra.v_head = kHeadDim;
+  ra.g = g; ra.g_tok = Hv; ra.g_head = 1;
+  ra.beta = beta; ra.b_tok = Hv; ra.b_head = 1;
+  ra.o = o; ra.o_tok = static_cast<int64_t>(Hv) * kHeadDim; ra.o_head = kHeadDim;
+  ra.state = state;
+  ra.B = B; ra.T = T; ra.Hk = Hk; ra.Hv = Hv;
+  ra.scale = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(kHeadDim));
+  ra.l2norm = use_qk_l2norm ? 1 : 0;
+  GDN_CUDA(recurrence_forward(ra, static_cast<cudaStream_t>(stream)));
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_gemm_bf16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int32_t m,
+                                    int32_t n, int32_t k, int32_t out_kind, void* out, int64_t ldo, int32_t ksplit,
+                                    void* stream) {
+  if (!a || !b || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_gemm_bf16: null argument");
+  if (m <= 0 || n <= 0 || k <= 0 || (k & 7) || lda < k || ldb < k)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_gemm_bf16: bad shape m=%d n=%d k=%d lda=%lld ldb=%lld", m, n, k,
+                static_cast<long long>(lda), static_cast<long long>(ldb));
+  if (out_kind < 0 || out_kind > 3) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_gemm_bf16: out_kind %d", out_kind);
+  if (ksplit < 0 || ksplit > 8) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_gemm_bf16: ksplit %d", ksplit);
+  const bool transposed = out_kind >= 2;
+  if (ldo < (transposed ? m : n)) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_gemm_bf16: ldo too small");
+  GemmEpiArgs ep;
+  ep.out = out;
+  ep.ld = ldo;
+  GDN_CUDA(gemm_bf16_tn(a, lda, b, ldb, m, n, k, out_kind, ep, ksplit, static_cast<cudaStream_t>(stream)));
+  return GDN_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Communicator
+// ------------------------------------------------------------------------------------------------
+extern "C" gdn_status gdn_comm_get_unique_id(void* id_out, size_t id_bytes) {
+  if (!id_out) return fail(GDN_ERR_NULL_POINTER, "gdn_comm_get_unique_id: null output");
+  if (id_bytes < sizeof(ncclUniqueId)) return fail(GDN_ERR_INVALID_ARGUMENT, "id buffer needs %zu bytes", sizeof(ncclUniqueId));
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  ncclResult_t r = api.getUniqueId(&id);
+  if (r != ncclSuccess) return fail(GDN_ERR_NCCL, "ncclGetUniqueId: %s", api.getErrorString(r));
+  memcpy(id_out, &id, sizeof(id));
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_comm_create(const void* id, size_t id_bytes, int32_t rank, int32_t world, gdn_comm** out) {
+  if (!id || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_comm_create: null argument");
+  *out = nullptr;
+  if (id_bytes < sizeof(ncclUniqueId)) return fail(GDN_ERR_INVALID_ARGUMENT, "id needs %zu bytes", sizeof(ncclUniqueId));
+  if (world <= 0 || rank < 0 || rank >= world) return fail(GDN_ERR_INVALID_ARGUMENT, "rank %d / world %d", rank, world);
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  gdn_comm* c = new (std::nothrow) gdn_comm();
+  if (!c) return fail(GDN_ERR_OUT_OF_MEMORY, "host allocation failed");
+  ncclResult_t r = api.commInitRank(&c->comm, world, uid, rank);
+  if (r != ncclSuccess) {
+    delete c;
+    return fail(GDN_ERR_NCCL, "ncclCommInitRank: %s", api.getErrorString(r));
+  }
+  c->rank = rank;
+  c->world = world;
+  *out = c;
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_comm_destroy(gdn_comm* c) {
+  if (!c) return fail(GDN_ERR_NULL_POINTER, "gdn_comm_destroy: null communicator");
+  const NcclApi& api = nccl();
+  if (api.ok && c->comm) api.commDestroy(c->comm);
+  delete c;
+  return GDN_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Misc
+// ------------------------------------------------------------------------------------------------
+extern "C" gdn_status gdn_device_error(int32_t* code_out) {
+  if (!code_out) return fail(GDN_ERR_NULL_POINTER, "gdn_device_error: null output");
+  GDN_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  GDN_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  const int zero = 0;
+  GDN_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  *code_out = v;
+  if (v != 0) return fail(GDN_ERR_TIMEOUT, "device error word 0x%x (a bounded wait expired)", v);
+  return GDN_OK;
+}
+
+extern "C" const char* gdn_last_error_string(void) { return t_last_error.c_str(); }
+
+extern "C" uint64_t gdn_kernel_launch_count(void) { return launch_count(); }
+
+extern "C" int32_t gdn_abi_version(void) { return GDN_ABI_VERSION; }

@@ -1,0 +1,393 @@
+// tcgen05 GEMM for sm_100a: C = A * B^T with A [M, K] and B [N, K] bf16 K-major, fp32 accumulators in
+// TMEM.  One CTA computes one 128 x BN tile (or one K-slice of it):
+//   warp 0      TMA producer (one elected lane), STAGES-deep ring of 128B-swizzled A/B tiles
+//   warp 1      TMEM allocator and UMMA issuer (one elected lane), commits free stages back to warp 0
+//   warps 2..5  epilogue: tcgen05.ld of the 32-lane TMEM quarter (warp % 4) -> fused epilogue -> global
+// Split-K (skinny decode GEMMs) runs the K-slices of a tile as one thread-block cluster; the slices'
+// fp32 partial tiles are summed by the leader CTA through distributed shared memory.
+//
+// The two GEMMs of the layer use it as:
+//   in_proj  (9B/gdn_layer.py:255-259: ttnn.linear for qkv+z and for a,b) fused into ONE weight
+//            [q | k | v | z | a | b] x hidden; decode swaps the operands (weights are A) and fuses the
+//            causal conv, the conv-state roll and the gating scalars into the epilogue;
+//   out_proj (9B/gdn_layer.py:272-276).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace gdn {
+
+__device__ int g_device_error = 0;
+
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launch_count() { return g_launches.load(); }
+void count_launch() { g_launches.fetch_add(1); }
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int kGemmThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + 1 KB alignment slack
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M = 128");
+  static_assert(BN * kBM * 4 <= STAGES * kStageBytes, "split-K partial tile must fit in the stage ring");
+};
+
+template <int EPI>
+__device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0, int M, int N,
+                                           const float (&v)[16]) {
+  if (m >= M) return;
+  if constexpr (EPI == kEpiStoreF32) {
+    float* row = static_cast<float*>(ep.out) + static_cast<int64_t>(m) * ep.ld + n0;
+    if (n0 + 16 <= N && (ep.ld & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(row)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) row[j] = v[j];
+    }
+  } else if constexpr (EPI == kEpiStoreBF16) {
+    __nv_bfloat16* row = static_cast<__nv_bfloat16*>(ep.out) + static_cast<int64_t>(m) * ep.ld + n0;
+    if (n0 + 16 <= N && (ep.ld & 7) == 0) {
+      uint4 pk[2];
+      uint32_t* w = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      reinterpret_cast<uint4*>(row)[0] = pk[0];
+      reinterpret_cast<uint4*>(row)[1] = pk[1];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) row[j] = __float2bfloat16_rn(v[j]);
+    }
+  } else if constexpr (EPI == kEpiStoreF32T) {
+    float* out = static_cast<float*>(ep.out);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = v[j];
+  } else if constexpr (EPI == kEpiStoreBF16T) {
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(ep.out);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = __float2bfloat16_rn(v[j]);
+  } else {  // kEpiDecodeInProj
+    float* out = static_cast<float*>(ep.out);
+    const int cr = ep.conv_rows;
+    if (m < cr) {
+      // Causal conv over the last 3 inputs (conv_state rows 0..2, oldest first) and this token; the
+      // state rolls by one (9B/kernels/layer_reader.cpp:184-197; HF torch_causal_conv1d_update).
+      const float4 w = *reinterpret_cast<const float4*>(ep.conv_w + static_cast<int64_t>(m) * 4);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + j;
+        if (n < N) {
+          float* cs = ep.conv_state + static_cast<int64_t>(n) * 3 * cr + m;
+          const float s0 = cs[0], s1 = cs[cr], s2 = cs[2 * cr], x = v[j];
+          cs[0] = s1;
+          cs[cr] = s2;
+          cs[2 * cr] = x;
+          out[static_cast<int64_t>(n) * ep.ld + m] = silu_f(w.x * s0 + w.y * s1 + w.z * s2 + w.w * x);
+        }
+      }
+    } else if (m < cr + ep.z_rows) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = v[j];
+    } else if (m < cr + ep.z_rows + ep.nheads) {
+      // g = -exp(A_log) * softplus(a + dt_bias)   (9B/kernels/layer_compute.cpp:160-166)
+      const int h = m - cr - ep.z_rows;
+      const float neg_a = -expf(ep.a_log[h]), dtb = ep.dt_bias[h];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = neg_a * softplus_f(v[j] + dtb);
+    } else {
+      // beta = sigmoid(b)   (layer_compute.cpp:176-177)
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = sigmoid_f(v[j]);
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, int ksplit, int n_tiles, int group_m, GemmEpiArgs ep) {
+  using C = GemmCfg<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x / ksplit, split = blockIdx.x % ksplit;
+  // Grouped rasterisation: group_m consecutive M tiles sweep all N tiles, so the A and B tiles a wave
+  // touches stay in L2.
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int per_group = group_m * n_tiles;
+  const int first_m = (tile / per_group) * group_m;
+  const int gsize = min(m_tiles - first_m, group_m);
+  const int m_tile = first_m + (tile % per_group) % gsize;
+  const int n_tile = (tile % per_group) / gsize;
+  const int kblocks = (K + kBK - 1) / kBK;
+  const int kb0 = static_cast<int>(static_cast<int64_t>(split) * kblocks / ksplit);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * kblocks / ksplit);
+  const int nk = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      // Decode (transposed epilogues): A is the weight matrix, streamed exactly once.
+      const bool a_streamed = EPI == kEpiStoreF32T || EPI == kEpiStoreBF16T || EPI == kEpiDecodeInProj;
+      const uint64_t pol_a = a_streamed ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_b = policy_evict_last();
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, kErrWaitSmemEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+        const int kx = (kb0 + i) * kBK;
+        tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kx, m_tile * kBM, pol_a);
+        tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kx, n_tile * BN, pol_b);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_dense(1, kBM, BN);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&full[s], (i / STAGES) & 1, kErrWaitTmaFull)) break;
+        tc_fence_after();
+        const uint64_t da = sdesc_k_sw128(smem_u32(sA + s * C::kABytes));
+        const uint64_t db = sdesc_k_sw128(smem_u32(sB + s * C::kBBytes));
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)  // +32 bytes along K inside the swizzle row = +2 in the descriptor
+          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+    __syncwarp();
+  }
+
+  const int q = warp & 3;          // TMEM lane quarter this warp may access
+  const int r = q * 32 + lane;     // row inside the tile
+  const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
+  const bool epi_warp = warp >= 2;
+  if (epi_warp) {
+    mbar_wait(accum, 0, kErrWaitAccum);
+    tc_fence_after();
+  }
+  if (ksplit > 1) {
+    if (epi_warp && split != 0) {
+      // Non-leader slices park their partial tile in their own (now idle) stage ring.
+      float4* part = reinterpret_cast<float4*>(smem);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(t_row + c0, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          part[(c0 / 4 + i) * kBM + r] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    __syncwarp();
+    cluster_sync();
+  }
+  if (epi_warp && split == 0) {
+    const int m = m_tile * kBM + r;
+    const uint32_t part_addr = smem_u32(smem);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16];
+      tmem_ld16(t_row + c0, v);
+#pragma unroll 1
+      for (int rank = 1; rank < ksplit; ++rank) {
+        const uint32_t base = mapa_shared(part_addr, rank);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 p = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
+          v[4 * i] += p.x;
+          v[4 * i + 1] += p.y;
+          v[4 * i + 2] += p.z;
+          v[4 * i + 3] += p.w;
+        }
+      }
+      epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
+    }
+  }
+  if (ksplit > 1) {
+    __syncwarp();
+    cluster_sync();  // peers keep their shared memory until the leader has read it
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] with row stride ld, tiles of 64 (K) x box_rows, 128B swizzle.
+static cudaError_t make_tmap(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                             int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * 2) & 15) || rows <= 0 || cols <= 0 || ld < cols)
+    return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int BN, int STAGES, int EPI>
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit,
+                               const GemmEpiArgs& ep, cudaStream_t stream) {
+  using C = GemmCfg<BN, STAGES>;
+  auto kern = gemm_tn_kernel<BN, STAGES, EPI>;
+  static bool attr_set = false;  // per instantiation; the attribute is per-device-context but idempotent
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  attr_set = true;
+  (void)attr_set;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
+  const int group_m = std::min(16, m_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * ksplit));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(ksplit);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ksplit > 1 ? 1 : 0;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, n_tiles, group_m, ep);
+}
+
+template <int BN, int STAGES>
+static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                                int ksplit, const GemmEpiArgs& ep, cudaStream_t s) {
+  switch (epi) {
+    case kEpiStoreF32: return launch_gemm<BN, STAGES, kEpiStoreF32>(ta, tb, M, N, K, ksplit, ep, s);
+    case kEpiStoreBF16: return launch_gemm<BN, STAGES, kEpiStoreBF16>(ta, tb, M, N, K, ksplit, ep, s);
+    case kEpiStoreF32T: return launch_gemm<BN, STAGES, kEpiStoreF32T>(ta, tb, M, N, K, ksplit, ep, s);
+    case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T>(ta, tb, M, N, K, ksplit, ep, s);
+    case kEpiDecodeInProj: return launch_gemm<BN, STAGES, kEpiDecodeInProj>(ta, tb, M, N, K, ksplit, ep, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+static int pick_ksplit(int tiles, int kblocks, int num_sms) {
+  if (tiles >= num_sms) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int ks = 1; ks <= 8 && ks <= kblocks; ++ks) {
+    const int ctas = tiles * ks;
+    const int waves = (ctas + num_sms - 1) / num_sms;
+    const double eff = static_cast<double>(ctas) / (static_cast<double>(waves) * num_sms);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = ks;
+    }
+  }
+  return best;
+}
+
+static int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
+                         const GemmEpiArgs& ep, int ksplit, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || (K & 7)) return cudaErrorInvalidValue;
+  int BN;
+  if (N <= 16) BN = 16;
+  else if (N <= 32) BN = 32;
+  else if (N <= 64) BN = 64;
+  else if (N <= 128) BN = 128;
+  else BN = 256;
+  CUtensorMap ta, tb;
+  cudaError_t e = make_tmap(&ta, A, M, K, lda, kBM);
+  if (e != cudaSuccess) return e;
+  e = make_tmap(&tb, B, N, K, ldb, BN);
+  if (e != cudaSuccess) return e;
+  const int kblocks = (K + kBK - 1) / kBK;
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  if (ksplit <= 0) ksplit = pick_ksplit(tiles, kblocks, sm_count());
+  ksplit = std::max(1, std::min(ksplit, std::min(8, kblocks)));
+  switch (BN) {
+    case 16: return dispatch_epi<16, 8>(epi, ta, tb, M, N, K, ksplit, ep, stream);
+    case 32: return dispatch_epi<32, 8>(epi, ta, tb, M, N, K, ksplit, ep, stream);
+    case 64: return dispatch_epi<64, 8>(epi, ta, tb, M, N, K, ksplit, ep, stream);
+    case 128: return dispatch_epi<128, 6>(epi, ta, tb, M, N, K, ksplit, ep, stream);
+    default: return dispatch_epi<256, 4>(epi, ta, tb, M, N, K, ksplit, ep, stream);
+  }
+}
+
+}  // namespace gdn

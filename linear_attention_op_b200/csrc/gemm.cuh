@@ -1,0 +1,45 @@
+// Internal interface of the tcgen05 GEMM (C = A * B^T, bf16 operands, fp32 accumulation in TMEM).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+// What the epilogue does with the fp32 accumulator tile.
+enum GemmEpi : int {
+  kEpiStoreF32 = 0,      // out[m * ld + n] = acc
+  kEpiStoreBF16 = 1,     // out[m * ld + n] = bf16(acc)
+  kEpiStoreF32T = 2,     // out[n * ld + m] = acc          (A = weights, B = activations)
+  kEpiStoreBF16T = 3,    // out[n * ld + m] = bf16(acc)
+  kEpiDecodeInProj = 4,  // transposed store of the fused in_proj of one decode token per sequence:
+                         //   rows [0, conv_rows): causal conv (K = 4) + SiLU, rolls conv_state
+                         //   rows [conv_rows, conv_rows + z_rows): plain
+                         //   next nheads rows: g = -exp(A_log) softplus(a + dt_bias)
+                         //   next nheads rows: beta = sigmoid(b)
+};
+
+struct GemmEpiArgs {
+  void* out = nullptr;
+  int64_t ld = 0;  // leading dimension of `out`, in elements
+  // kEpiDecodeInProj only
+  int conv_rows = 0;
+  int z_rows = 0;
+  int nheads = 0;
+  const float* conv_w = nullptr;  // [conv_rows, 4]
+  float* conv_state = nullptr;    // [N, 3, conv_rows] (N = number of sequences = GEMM N)
+  const float* a_log = nullptr;   // [nheads]
+  const float* dt_bias = nullptr; // [nheads]
+};
+
+// A: [M, K] bf16 row-major with row stride lda (elements); B: [N, K] bf16 row-major with row stride ldb.
+// ksplit > 1 splits K over a cluster of ksplit CTAs whose partial tiles are summed through
+// distributed shared memory (no global workspace).  ksplit = 0 picks a value.
+cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
+                         const GemmEpiArgs& args, int ksplit, cudaStream_t stream);
+
+// Number of kernel launches issued by this library since load (for the benchmark's launch count).
+uint64_t launch_count();
+void count_launch();
+
+}  // namespace gdn

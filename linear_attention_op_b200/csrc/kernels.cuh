@@ -1,0 +1,65 @@
+// Internal interface of the non-GEMM kernels (recurrence, conv, chunked prefill).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int kHeadDim = 128;  // dk = dv = 128 (the Qwen3.5 GDN head size; the only one supported)
+
+// Strided views of the per-token inputs of the recurrence.  Element (row, head, i) of a vector input lives
+// at ptr[row * tok + head * head_stride + i]; row = b * T + t (sequence-major).
+struct RecurrenceArgs {
+  const float* q = nullptr;
+  int64_t q_tok = 0, q_head = 0;  // indexed by k-head
+  const float* k = nullptr;
+  int64_t k_tok = 0, k_head = 0;  // indexed by k-head
+  const float* v = nullptr;
+  int64_t v_tok = 0, v_head = 0;
+  const float* g = nullptr;  // log decay
+  int64_t g_tok = 0, g_head = 0;
+  const float* beta = nullptr;
+  int64_t b_tok = 0, b_head = 0;
+  // Gated RMSNorm epilogue (when z != nullptr): y = RMSNorm(o) * norm_w * SiLU(z) -> bf16
+  const float* z = nullptr;
+  int64_t z_tok = 0, z_head = 0;
+  const float* norm_w = nullptr;  // [128]
+  float eps = 1e-6f;
+  void* y = nullptr;  // bf16
+  int64_t y_tok = 0, y_head = 0;
+  // Raw output (when z == nullptr): o fp32
+  float* o = nullptr;
+  int64_t o_tok = 0, o_head = 0;
+  float* state = nullptr;  // [B, Hv, 128, 128] fp32, in place
+  int B = 0, T = 0, Hk = 0, Hv = 0;
+  float scale = 0.0f;  // q scale (dk^-0.5 by default)
+  int l2norm = 1;
+};
+
+// Token-by-token gated delta rule, one CTA per (sequence, v-head), state kept in registers.
+cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream);
+
+// Prefill causal conv (K = 4) + SiLU: in[row * in_ld + c] pre-conv channels c < C, out[row * out_ld + c].
+// conv_state [B, 3, C] supplies the history before t = 0 and is then rolled to the last 3 inputs.
+cudaError_t conv_prefill(const float* in, int64_t in_ld, float* out, int64_t out_ld, const float* conv_w,
+                         float* conv_state, int B, int T, int C, cudaStream_t stream);
+
+// Chunked prefill of the whole recurrence + gated RMSNorm over the layer's in_proj output.
+struct ChunkArgs {
+  const float* qkv = nullptr;  // post-conv q | k | v, [B*T, qkv_ld]
+  int64_t qkv_ld = 0;
+  const float* proj = nullptr;  // in_proj output rows [B*T, proj_ld]: z at z_off, a at a_off, b at b_off
+  int64_t proj_ld = 0;
+  int64_t z_off = 0, a_off = 0, b_off = 0;
+  const float* a_log = nullptr;
+  const float* dt_bias = nullptr;
+  const float* norm_w = nullptr;
+  float eps = 1e-6f;
+  float* state = nullptr;  // [B, Hv, 128, 128]
+  void* y = nullptr;       // bf16 [B*T, Hv*128]
+  int B = 0, T = 0, Hk = 0, Hv = 0;
+};
+cudaError_t chunk_prefill(const ChunkArgs& a, cudaStream_t stream);
+
+}  // namespace gdn

@@ -1,0 +1,144 @@
+// Token-by-token gated delta rule (decode, and the recurrence-only op).
+//
+// Math per (sequence b, v-head h, token t), fp32 (9B/reference.py:28-34; 9B/kernels/gdn_compute.cpp:51-122):
+//   q^ = q rsqrt(|q|^2 + 1e-6) * scale,  k^ = k rsqrt(|k|^2 + 1e-6)        (GQA: k-head = h / (Hv/Hk))
+//   S' = exp(g) S;   u = beta (v - S'^T k^);   S <- S' + k^ u^T;   o = S^T q^ = S'^T q^ + (q^.k^) u
+// One CTA of 256 threads owns the 128 x 128 fp32 state of one (b, h).  Thread t holds rows
+// 16*(t/32) .. +15 of the column quad 4*(t%32) .. +3 in registers, so every warp moves 512 contiguous
+// bytes per row and the state is read once and written once per call.  S^T k and S^T q come out of one
+// pass (partials per row group reduced through shared memory); the output is either raw o or the gated
+// RMSNorm y = RMSNorm(o) * w * SiLU(z) in bf16 (9B/kernels/layer_compute.cpp:287-395).
+#include <cuda_bf16.h>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace gdn {
+
+constexpr int kRecThreads = 256;
+
+__global__ void __launch_bounds__(kRecThreads, 2) recurrence_kernel(RecurrenceArgs a) {
+  const int b = blockIdx.x / a.Hv, h = blockIdx.x % a.Hv;
+  const int kh = h / (a.Hv / a.Hk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = lane * 4;    // first of this thread's 4 columns
+  const int r0 = warp * 16;   // first of this thread's 16 rows
+
+  __shared__ float s_q[kHeadDim], s_k[kHeadDim], s_v[kHeadDim], s_z[kHeadDim];
+  __shared__ float s_u[kHeadDim], s_o[kHeadDim];
+  __shared__ float4 s_rk[8][32], s_rq[8][32];  // per row-group partials of S'^T k and S'^T q
+  __shared__ float s_red[4][4];
+  __shared__ float s_scal[2];
+
+  float* S = a.state + (static_cast<int64_t>(b) * a.Hv + h) * kHeadDim * kHeadDim;
+  float4 st[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    st[i] = __ldcs(reinterpret_cast<const float4*>(S + (r0 + i) * kHeadDim + c0));
+
+#pragma unroll 1
+  for (int t = 0; t < a.T; ++t) {
+    const int64_t row = static_cast<int64_t>(b) * a.T + t;
+    // ---- load the token's vectors and reduce |q|^2, |k|^2, q.k (warps 0..3, one element per thread)
+    if (tid < kHeadDim) {
+      const float qv = a.q[row * a.q_tok + kh * a.q_head + tid];
+      const float kv = a.k[row * a.k_tok + kh * a.k_head + tid];
+      s_q[tid] = qv;
+      s_k[tid] = kv;
+      s_v[tid] = a.v[row * a.v_tok + h * a.v_head + tid];
+      if (a.z) s_z[tid] = a.z[row * a.z_tok + h * a.z_head + tid];
+      float sq = qv * qv, sk = kv * kv, sqk = qv * kv;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        sk += __shfl_xor_sync(0xffffffffu, sk, off);
+        sqk += __shfl_xor_sync(0xffffffffu, sqk, off);
+      }
+      if (lane == 0) {
+        s_red[warp][0] = sq;
+        s_red[warp][1] = sk;
+        s_red[warp][2] = sqk;
+      }
+    } else if (tid == kHeadDim) {
+      s_scal[0] = expf(a.g[row * a.g_tok + h * a.g_head]);
+      s_scal[1] = a.beta[row * a.b_tok + h * a.b_head];
+    }
+    __syncthreads();
+    const float sq = s_red[0][0] + s_red[1][0] + s_red[2][0] + s_red[3][0];
+    const float sk = s_red[0][1] + s_red[1][1] + s_red[2][1] + s_red[3][1];
+    const float sqk = s_red[0][2] + s_red[1][2] + s_red[2][2] + s_red[3][2];
+    const float rq = a.l2norm ? rsqrtf(sq + 1e-6f) * a.scale : a.scale;
+    const float rk = a.l2norm ? rsqrtf(sk + 1e-6f) : 1.0f;
+    const float qk = sqk * rq * rk;
+    const float d = s_scal[0], beta = s_scal[1];
+
+    // ---- decay and the two projections over this thread's 16 rows
+    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float kr = s_k[r0 + i] * rk, qr = s_q[r0 + i] * rq;
+      float4& s = st[i];
+      s.x *= d;
+      s.y *= d;
+      s.z *= d;
+      s.w *= d;
+      pk.x += kr * s.x; pk.y += kr * s.y; pk.z += kr * s.z; pk.w += kr * s.w;
+      pq.x += qr * s.x; pq.y += qr * s.y; pq.z += qr * s.z; pq.w += qr * s.w;
+    }
+    s_rk[warp][lane] = pk;
+    s_rq[warp][lane] = pq;
+    __syncthreads();
+    if (tid < kHeadDim) {
+      const int quad = tid >> 2, comp = tid & 3;
+      float ks = 0.f, qs = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        ks += reinterpret_cast<const float*>(&s_rk[w][quad])[comp];
+        qs += reinterpret_cast<const float*>(&s_rq[w][quad])[comp];
+      }
+      const float u = beta * (s_v[tid] - ks);
+      const float o = qs + qk * u;
+      s_u[tid] = u;
+      s_o[tid] = o;
+      float so = o * o;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) so += __shfl_xor_sync(0xffffffffu, so, off);
+      if (lane == 0) s_red[warp][3] = so;
+    }
+    __syncthreads();
+    // ---- rank-1 update of the state
+    const float4 u4 = *reinterpret_cast<const float4*>(&s_u[c0]);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float kr = s_k[r0 + i] * rk;
+      st[i].x += kr * u4.x;
+      st[i].y += kr * u4.y;
+      st[i].z += kr * u4.z;
+      st[i].w += kr * u4.w;
+    }
+    // ---- output
+    if (tid < kHeadDim) {
+      const float o = s_o[tid];
+      if (a.z) {
+        const float ms = (s_red[0][3] + s_red[1][3] + s_red[2][3] + s_red[3][3]) * (1.0f / kHeadDim);
+        const float y = o * rsqrtf(ms + a.eps) * a.norm_w[tid] * silu_f(s_z[tid]);
+        static_cast<__nv_bfloat16*>(a.y)[row * a.y_tok + h * a.y_head + tid] = __float2bfloat16_rn(y);
+      } else {
+        a.o[row * a.o_tok + h * a.o_head + tid] = o;
+      }
+    }
+    __syncthreads();  // shared vectors are rewritten by the next token
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) __stcs(reinterpret_cast<float4*>(S + (r0 + i) * kHeadDim + c0), st[i]);
+}
+
+cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream) {
+  if (a.B <= 0 || a.T <= 0 || a.Hk <= 0 || a.Hv <= 0 || a.Hv % a.Hk) return cudaErrorInvalidValue;
+  count_launch();
+  recurrence_kernel<<<a.B * a.Hv, kRecThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace gdn

@@ -1,0 +1,320 @@
+"""Host-side mirror of the reference's per-layer op API, on top of the C-ABI (``include/gdn_b200.h``).
+
+* ``Qwen35GatedDeltaNet``  <- ``Qwen35GatedDeltaNetTT`` (9B/gdn_layer.py:54-292): full layer, prefill and
+  decode, state kept on the device across calls, ``reset_state`` / ``get_recurrent_state``.
+* ``GDNStack``             <- ``Qwen35_08B_GDNStackL1`` (0.8B/gdn_l1.py:147-341): several layers back to
+  back with one state per layer, ``layers=[i]`` selection, ``allocate_activations`` / ``forward_into``
+  for CUDA-graph replay (the reference's trace capture, 0.8B/bench_decode.py:44-57).
+* ``GatedDeltaRule``       <- ``GatedDeltaRuleL1`` (9B/gated_delta_l1.py:131-272): the recurrence alone.
+
+Everything runs in libgdn_b200.so; PyTorch only provides device memory and the current stream.  Errors
+raise ``GDNError`` (the reference uses asserts / ValueError, which callers may also catch as RuntimeError).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import Dims, LayerInfo, Weights, call
+
+HEAD_DIM = 128
+
+
+def _stream_handle(stream: torch.cuda.Stream | None = None) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+@dataclass
+class LayerWeights:
+    """HF-layout weights of one layer (host or device tensors).  Projections are converted to bf16."""
+
+    w_qkv: torch.Tensor
+    w_z: torch.Tensor
+    w_a: torch.Tensor
+    w_b: torch.Tensor
+    conv_w: torch.Tensor  # [conv_dim, K]
+    a_log: torch.Tensor
+    dt_bias: torch.Tensor
+    norm_w: torch.Tensor
+    w_out: torch.Tensor
+    num_k_heads: int
+    num_v_heads: int
+    head_k_dim: int = HEAD_DIM
+    head_v_dim: int = HEAD_DIM
+    eps: float = 1e-6
+
+    @property
+    def hidden(self) -> int:
+        return int(self.w_qkv.shape[1])
+
+    @classmethod
+    def from_hf(cls, layer) -> "LayerWeights":
+        """From a Hugging Face ``Qwen3_5GatedDeltaNet`` (the reference's constructor argument)."""
+        g = lambda t: t.detach()
+        eps = getattr(layer.norm, "variance_epsilon", None) or getattr(layer, "layer_norm_epsilon", 1e-6)
+        return cls(g(layer.in_proj_qkv.weight), g(layer.in_proj_z.weight), g(layer.in_proj_a.weight),
+                   g(layer.in_proj_b.weight), g(layer.conv1d.weight)[:, 0, :], g(layer.A_log), g(layer.dt_bias),
+                   g(layer.norm.weight), g(layer.out_proj.weight), int(layer.num_k_heads), int(layer.num_v_heads),
+                   int(layer.head_k_dim), int(layer.head_v_dim), float(eps))
+
+    @classmethod
+    def from_any(cls, w) -> "LayerWeights":
+        if isinstance(w, cls):
+            return w
+        if hasattr(w, "in_proj_qkv"):
+            return cls.from_hf(w)
+        fields = ("w_qkv", "w_z", "w_a", "w_b", "conv_w", "a_log", "dt_bias", "norm_w", "w_out", "num_k_heads",
+                  "num_v_heads")
+        get = (lambda k: w[k]) if isinstance(w, dict) else (lambda k: getattr(w, k))
+        kw = {k: get(k) for k in fields}
+        for k in ("head_k_dim", "head_v_dim", "eps"):
+            try:
+                kw[k] = get(k)
+            except (KeyError, AttributeError):
+                pass
+        return cls(**kw)
+
+
+class _LayerHandle:
+    """Owns one gdn_layer* (this rank's head shard of one layer's weights, on the current device)."""
+
+    def __init__(self, weights: LayerWeights, tp_rank: int = 0, tp_size: int = 1):
+        w = weights
+        bf = lambda t: t.detach().to(torch.bfloat16).contiguous()
+        f32 = lambda t: t.detach().to(torch.float32).contiguous()
+        keep = dict(w_qkv=bf(w.w_qkv), w_z=bf(w.w_z), w_a=bf(w.w_a), w_b=bf(w.w_b), conv_w=f32(w.conv_w),
+                    a_log=f32(w.a_log), dt_bias=f32(w.dt_bias), norm_w=f32(w.norm_w), w_out=bf(w.w_out))
+        self.dims = Dims(w.hidden, w.num_k_heads, w.num_v_heads, w.head_k_dim, w.head_v_dim,
+                         int(keep["conv_w"].shape[1]), float(w.eps), 64)
+        cw = Weights(*(ctypes.c_void_p(keep[k].data_ptr()) for k in
+                       ("w_qkv", "w_z", "w_a", "w_b", "conv_w", "a_log", "dt_bias", "norm_w", "w_out")))
+        handle = ctypes.c_void_p()
+        call("gdn_layer_create", ctypes.byref(self.dims), ctypes.byref(cw), tp_rank, tp_size, ctypes.byref(handle))
+        self.handle = handle
+        self.info = LayerInfo()
+        call("gdn_layer_get_info", self.handle, ctypes.byref(self.info))
+        self.hidden = w.hidden
+
+    def reserve(self, max_tokens: int) -> None:
+        call("gdn_layer_reserve", self.handle, int(max_tokens))
+
+    def forward(self, x: torch.Tensor, B: int, T: int, rec: torch.Tensor, conv: torch.Tensor, out: torch.Tensor,
+                comm=None, stream=None) -> None:
+        call("gdn_layer_forward", self.handle, _ptr(x), B, T, _ptr(rec), _ptr(conv), _ptr(out),
+             ctypes.c_void_p(comm.handle.value if comm is not None else 0), _stream_handle(stream))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            _lib.lib().gdn_layer_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Qwen35GatedDeltaNet:
+    """One Gated DeltaNet layer on a B200, continuing from its on-device state across calls.
+
+    Drop-in for ``Qwen35GatedDeltaNetTT(device, hf_layer, batch)``: ``layer(x)`` with x ``[B, T, hidden]``
+    (any device/dtype) returns ``[B, T, hidden]`` on x's device in x's dtype; T == 1 is a decode step,
+    T > 1 a chunked prefill.  ``tp_rank``/``tp_size``/``comm`` shard the heads over GPUs (one NCCL
+    all-reduce per call); with ``tp_size > 1`` and ``comm=None`` the call returns this rank's partial sum.
+    """
+
+    def __init__(self, hf_layer=None, batch: int = 1, *, weights=None, device=None, tp_rank: int = 0,
+                 tp_size: int = 1, comm=None, max_rows: int | None = None):
+        if (hf_layer is None) == (weights is None):
+            raise ValueError("pass exactly one of hf_layer or weights")
+        if batch <= 0:
+            raise ValueError("batch must be > 0")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.batch = batch
+        self.comm = comm
+        w = LayerWeights.from_any(hf_layer if hf_layer is not None else weights)
+        with torch.cuda.device(self.device):
+            self._h = _LayerHandle(w, tp_rank, tp_size)
+        info = self._h.info
+        self.hidden = info.hidden
+        self.nk, self.nv = w.num_k_heads, w.num_v_heads
+        self.nk_local, self.nv_local = info.num_k_heads_local, info.num_v_heads_local
+        self.conv_dim_local = info.conv_dim_local
+        self.dk = self.dv = HEAD_DIM
+        if max_rows:
+            with torch.cuda.device(self.device):
+                self._h.reserve(max_rows)
+        self.reset_state()
+
+    # ---- state (9B/gdn_layer.py:137-157) -----------------------------------------------------------
+    def reset_state(self) -> None:
+        """Zero both states in place (their device addresses never change, so captured graphs stay valid)."""
+        B = self.batch
+        if getattr(self, "rec_state", None) is None:
+            self.rec_state = torch.zeros(B, self.nv_local, self.dk, self.dv, dtype=torch.float32, device=self.device)
+            self.conv_state = torch.zeros(B, 3, self.conv_dim_local, dtype=torch.float32, device=self.device)
+        else:
+            self.rec_state.zero_()
+            self.conv_state.zero_()
+
+    def set_state(self, rec_state: torch.Tensor | None = None, conv_state: torch.Tensor | None = None) -> None:
+        if rec_state is not None:
+            self.rec_state.copy_(rec_state.reshape(self.rec_state.shape))
+        if conv_state is not None:
+            self.conv_state.copy_(conv_state.reshape(self.conv_state.shape))
+
+    def get_recurrent_state(self) -> torch.Tensor:
+        """[B, Hv_local, dk, dv] host copy (for checks)."""
+        return self.rec_state.detach().float().cpu()
+
+    def get_conv_state(self) -> torch.Tensor:
+        """[B, 3, conv_dim_local] host copy: rows hold the last 3 pre-conv inputs, oldest first."""
+        return self.conv_state.detach().float().cpu()
+
+    # ---- forward -----------------------------------------------------------------------------------
+    def forward_into(self, x: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+        """Device bf16 x [B, T, hidden] -> device bf16 out (preallocated); allocates nothing once the
+        workspace is reserved, so it can be captured in a CUDA graph."""
+        B, T, H = x.shape
+        if B != self.batch or H != self.hidden:
+            raise ValueError(f"x is {tuple(x.shape)}, layer expects [{self.batch}, T, {self.hidden}]")
+        if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or not x.is_contiguous() or not out.is_contiguous():
+            raise ValueError("forward_into wants contiguous bf16 tensors")
+        self._h.forward(x, B, T, self.rec_state, self.conv_state, out, self.comm, stream)
+        return out
+
+    def __call__(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        B, T, H = hidden_states.shape
+        if B != self.batch or H != self.hidden:
+            raise ValueError(f"hidden_states is {tuple(hidden_states.shape)}, layer expects [{self.batch}, T, {self.hidden}]")
+        with torch.cuda.device(self.device):
+            x = hidden_states.to(device=self.device, dtype=torch.bfloat16).contiguous()
+            out = torch.empty_like(x)
+            self.forward_into(x, out)
+        return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+
+    def reserve(self, max_tokens: int) -> None:
+        with torch.cuda.device(self.device):
+            self._h.reserve(max_tokens)
+
+    def with_batch(self, batch: int) -> "Qwen35GatedDeltaNet":
+        """Another op over the same device weights (and workspace) with its own batch size and zeroed state.
+        The two ops must not run concurrently on different streams (they share the workspace)."""
+        other = object.__new__(Qwen35GatedDeltaNet)
+        other.__dict__.update({k: v for k, v in self.__dict__.items() if k not in ("rec_state", "conv_state")})
+        other.batch = batch
+        other.rec_state = other.conv_state = None
+        other.reset_state()
+        return other
+
+    def set_stage_events(self, events: list | None) -> None:
+        """Have every forward record up to 6 timing events at its stage boundaries (see
+        gdn_layer_set_stage_events); None disables."""
+        if not events:
+            call("gdn_layer_set_stage_events", self._h.handle, None, 0)
+            self._stage_events = None
+            return
+        for e in events:  # torch creates the CUDA event lazily on first record
+            e.record()
+        arr = (ctypes.c_void_p * len(events))(*[ctypes.c_void_p(e.cuda_event) for e in events])
+        call("gdn_layer_set_stage_events", self._h.handle, arr, len(events))
+        self._stage_events = (events, arr)
+
+
+class GDNStack:
+    """Several GDN layers run back to back, each with its own state (decode or prefill).
+
+    Drop-in for ``Qwen35_08B_GDNStackL1(device, hf_layers, batch)``: ``stack(x, layers=None)`` applies the
+    selected layers in order (GDN mixers only: no norms, residuals or MLP, like the reference)."""
+
+    def __init__(self, hf_layers, batch: int = 1, *, device=None, tp_rank: int = 0, tp_size: int = 1, comm=None,
+                 max_rows: int | None = None):
+        self.batch = batch
+        self.layers = [Qwen35GatedDeltaNet(weights=LayerWeights.from_any(L), batch=batch, device=device,
+                                           tp_rank=tp_rank, tp_size=tp_size, comm=comm, max_rows=max_rows)
+                       for L in hf_layers]
+        self.hidden = self.layers[0].hidden
+        self.device = self.layers[0].device
+
+    def reset_state(self) -> None:
+        for L in self.layers:
+            L.reset_state()
+
+    def get_recurrent_state(self, i: int) -> torch.Tensor:
+        return self.layers[i].get_recurrent_state()
+
+    def allocate_activations(self, seq_len: int = 1) -> list[torch.Tensor]:
+        """One persistent bf16 output buffer per layer, for forward_into / CUDA-graph capture."""
+        return [torch.empty(self.batch, seq_len, self.hidden, dtype=torch.bfloat16, device=self.device)
+                for _ in self.layers]
+
+    def forward_into(self, x: torch.Tensor, outs: list[torch.Tensor], stream=None) -> torch.Tensor:
+        for L, out in zip(self.layers, outs):
+            L.forward_into(x, out, stream)
+            x = out
+        return x
+
+    def __call__(self, hidden_states: torch.Tensor, layers=None) -> torch.Tensor:
+        shape = hidden_states.shape
+        x = hidden_states.reshape(self.batch, -1, shape[-1])
+        idx = range(len(self.layers)) if layers is None else layers
+        with torch.cuda.device(self.device):
+            cur = x.to(device=self.device, dtype=torch.bfloat16).contiguous()
+            for i in idx:
+                out = torch.empty_like(cur)
+                self.layers[i].forward_into(cur, out)
+                cur = out
+        return cur.reshape(shape).to(device=hidden_states.device, dtype=hidden_states.dtype)
+
+
+class GatedDeltaRule:
+    """The recurrence alone with its state resident on the device across calls.
+
+    Drop-in for ``GatedDeltaRuleL1(device, num_heads, head_k_dim, head_v_dim, initial_state=...)``:
+    ``op(q, k, v, g, beta, use_qk_l2norm=True, scale=None)`` with q, k ``[B, T, Hk, dk]``, v
+    ``[B, T, Hv, dv]``, g, beta ``[B, T, Hv]`` returns o ``[B, T, Hv, dv]``; ``num_heads`` = B * Hv."""
+
+    def __init__(self, num_heads: int, head_k_dim: int = HEAD_DIM, head_v_dim: int = HEAD_DIM, *, device=None,
+                 initial_state: torch.Tensor | None = None):
+        if head_k_dim != HEAD_DIM or head_v_dim != HEAD_DIM:
+            raise ValueError("only head dims of 128 are supported")
+        self.num_heads = num_heads
+        self.dk, self.dv = head_k_dim, head_v_dim
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.state = torch.zeros(num_heads, self.dk, self.dv, dtype=torch.float32, device=self.device)
+        self.reset_state(initial_state)
+
+    def reset_state(self, initial_state: torch.Tensor | None = None) -> None:
+        """Reset in place (the buffer address never changes, like the reference's L1 state)."""
+        if initial_state is None:
+            self.state.zero_()
+        else:
+            self.state.copy_(initial_state.reshape(self.state.shape))
+
+    def get_state(self) -> torch.Tensor:
+        """[num_heads, dk, dv] host copy (for checks)."""
+        return self.state.detach().cpu()
+
+    def __call__(self, q, k, v, g, beta, use_qk_l2norm: bool = True, scale: float | None = None) -> torch.Tensor:
+        B, T, Hk, dk = q.shape
+        Hv = v.shape[2]
+        if B * Hv != self.num_heads or dk != self.dk or v.shape[3] != self.dv or Hv % Hk:
+            raise ValueError(f"shapes q {tuple(q.shape)} v {tuple(v.shape)} do not match num_heads={self.num_heads}")
+        dev = lambda t: t.to(device=self.device, dtype=torch.float32).contiguous()
+        with torch.cuda.device(self.device):
+            qd, kd, vd, gd, bd = dev(q), dev(k), dev(v), dev(g), dev(beta)
+            o = torch.empty(B, T, Hv, self.dv, dtype=torch.float32, device=self.device)
+            call("gdn_recurrence_forward", _ptr(qd), _ptr(kd), _ptr(vd), _ptr(gd), _ptr(bd), B, T, Hk, Hv,
+                 1 if use_qk_l2norm else 0, float(scale) if scale else 0.0, _ptr(self.state), _ptr(o),
+                 _stream_handle())
+        return o.to(q.device)
