@@ -25,8 +25,8 @@ __global__ void __launch_bounds__(kRecThreads, 2) recurrence_kernel(RecurrenceAr
   const int c0 = lane * 4;    // first of this thread's 4 columns
   const int r0 = warp * 16;   // first of this thread's 16 rows
 
-  __shared__ float s_q[kHeadDim], s_k[kHeadDim], s_v[kHeadDim], s_z[kHeadDim];
-  __shared__ float s_u[kHeadDim], s_o[kHeadDim];
+  __shared__ __align__(16) float s_q[kHeadDim], s_k[kHeadDim], s_v[kHeadDim], s_z[kHeadDim];
+  __shared__ __align__(16) float s_u[kHeadDim], s_o[kHeadDim];  // s_u is read as float4
   __shared__ float4 s_rk[8][32], s_rq[8][32];  // per row-group partials of S'^T k and S'^T q
   __shared__ float s_red[4][4];
   __shared__ float s_scal[2];
