@@ -119,6 +119,19 @@ GDN_API gdn_status gdn_layer_forward(gdn_layer* layer, const uint16_t* x, int32_
  * measures the same per-op split with its device profiler (9B/README.md:137-145). */
 GDN_API gdn_status gdn_layer_set_stage_events(gdn_layer* layer, void* const* events, int32_t count);
 
+/* One decode step (seq_len 1) that allocates no device memory, for callers that cannot call cudaMalloc
+ * during a call: code running inside a memory budget owned by another runtime, or code issuing calls while
+ * a stream is being captured (an allocation there breaks the capture).  No counterpart in the reference.
+ * Same math, inputs and outputs as gdn_layer_forward with seq_len = 1 and comm = NULL (with tp_size > 1, out
+ * holds this rank's partial sum).  The step's intermediates live in a static device array of 8 MiB that
+ * every GPU loading this library keeps until exit; a batch whose intermediates do not fit
+ * (batch * (4 * proj_ld + 2 * Hv_local * 128) bytes, about 145 sequences for the 9B geometry) is rejected
+ * with GDN_ERR_INVALID_ARGUMENT.  The first call on each device looks up the array's device address; make
+ * that first call before any stream capture.  All calls share the one array: calls whose GPU work overlaps
+ * (different streams, or different layers on concurrent streams) race on it. */
+GDN_API gdn_status gdn_layer_decode_static(gdn_layer* layer, const uint16_t* x, int32_t batch, float* rec_state,
+                                           float* conv_state, uint16_t* out, void* stream);
+
 /* Recurrence only (no projections, conv or norm), token by token, state updated in place:
  *   q, k fp32 [B, T, Hk, 128]; v fp32 [B, T, Hv, 128]; g (log decay), beta fp32 [B, T, Hv];
  *   state fp32 [B, Hv, 128, 128]; o fp32 [B, T, Hv, 128].

@@ -361,6 +361,96 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   return GDN_OK;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Decode step with static scratch (gdn_layer_decode_static)
+//
+// For callers that must not allocate device memory during a call: code running inside a memory budget
+// owned by someone else (a serving runtime's pool, an embedded host without allocator access), or code
+// that issues calls while a stream is being captured, where a cudaMalloc would break the capture.  The
+// step's two intermediates -- the fused in_proj output (fp32 [B, proj_ld]) and the gated-RMSNorm output
+// (bf16 [B, vd]) -- live in the file-scope array below instead of the layer workspace.  Every GPU that
+// loads this library holds the array until the process exits.
+// ------------------------------------------------------------------------------------------------
+static constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+
+static constexpr int kMaxDevices = 64;
+static void* g_scratch_addr[kMaxDevices] = {};
+static std::mutex g_scratch_mu;
+
+// Device address of g_decode_scratch on the current device, looked up once per device (the host-side
+// symbol is only a stand-in and must never be handed to a kernel).
+static gdn_status static_scratch(void** out) {
+  int dev = 0;
+  GDN_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(GDN_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    GDN_CUDA(cudaGetSymbolAddress(&p, g_decode_scratch));
+    if (!p) return fail(GDN_ERR_CUDA, "cudaGetSymbolAddress returned null for the static scratch");
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_layer_decode_static(gdn_layer* L, const uint16_t* x, int32_t B, float* rec_state,
+                                              float* conv_state, uint16_t* out, void* stream_ptr) {
+  if (!L || !x || !rec_state || !conv_state || !out)
+    return fail(GDN_ERR_NULL_POINTER, "gdn_layer_decode_static: null argument");
+  if (B <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_layer_decode_static: batch %d must be > 0", B);
+  if (!aligned16(x) || !aligned16(out) || !aligned16(rec_state) || !aligned16(conv_state))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_layer_decode_static: tensors must be 16-byte aligned");
+  const size_t proj_bytes = align256(static_cast<size_t>(B) * L->proj_ld * 4);
+  const size_t need = proj_bytes + align256(static_cast<size_t>(B) * L->vd * 2);
+  if (need > kStaticScratchBytes)
+    return fail(GDN_ERR_INVALID_ARGUMENT,
+                "gdn_layer_decode_static: batch %d needs %zu bytes of scratch, the static array holds %zu "
+                "(at most %zu sequences for this layer)",
+                B, need, kStaticScratchBytes,
+                kStaticScratchBytes / (static_cast<size_t>(L->proj_ld) * 4 + static_cast<size_t>(L->vd) * 2));
+  void* base = nullptr;
+  gdn_status st = static_scratch(&base);
+  if (st != GDN_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int h = L->dims.hidden;
+  float* proj = static_cast<float*>(base);
+  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(base) + proj_bytes);
+  const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
+  GemmEpiArgs ep;
+  ep.out = proj;
+  ep.ld = L->proj_ld;
+  ep.conv_rows = L->conv_dim;
+  ep.z_rows = L->vd;
+  ep.nheads = L->hv;
+  ep.conv_w = L->conv_w;
+  ep.conv_state = conv_state;
+  ep.a_log = L->a_log;
+  ep.dt_bias = L->dt_bias;
+  GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream));
+  RecurrenceArgs ra;
+  ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
+  ra.k = proj + L->kd; ra.k_tok = L->proj_ld; ra.k_head = kHeadDim;
+  ra.v = proj + 2 * L->kd; ra.v_tok = L->proj_ld; ra.v_head = kHeadDim;
+  ra.z = proj + z_off; ra.z_tok = L->proj_ld; ra.z_head = kHeadDim;
+  ra.g = proj + a_off; ra.g_tok = L->proj_ld; ra.g_head = 1;
+  ra.beta = proj + b_off; ra.b_tok = L->proj_ld; ra.b_head = 1;
+  ra.norm_w = L->norm_w;
+  ra.eps = L->dims.eps;
+  ra.y = y; ra.y_tok = L->vd; ra.y_head = kHeadDim;
+  ra.state = rec_state;
+  ra.B = B; ra.T = 1; ra.Hk = L->hk; ra.Hv = L->hv;
+  ra.scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
+  ra.l2norm = 1;
+  GDN_CUDA(recurrence_forward(ra, stream));
+  GemmEpiArgs eo;
+  eo.out = out;
+  eo.ld = h;
+  GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream));
+  return GDN_OK;
+}
+
 extern "C" gdn_status gdn_recurrence_forward(const float* q, const float* k, const float* v, const float* g,
                                              const float* beta, int32_t B, int32_t T, int32_t Hk, int32_t Hv,
                                              int32_t use_qk_l2norm, float scale, float* state, float* o,
