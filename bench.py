@@ -32,8 +32,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "GDN layer tokens/s (decode & 8K prefill), % HBM/tensor roofline, 1-8 B200"
 H, HK, HV, D = 4096, 16, 32, 128          # Qwen3.5-9B GDN geometry
-DECODE_B = 64                              # config 2
-PREFILL_B, PREFILL_T = 8, 8192             # config 3
+DECODE_B = 64                              # config 2 (override: --decode-b, for profiling smaller cases)
+PREFILL_B, PREFILL_T = 8, 8192             # config 3 (override: --prefill-b / --prefill-t)
+STAGES = ["in_proj", "conv", "chunk_prep", "recurrence", "out_proj", "allreduce"]
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -115,8 +116,12 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
+            t0 = time.time()  # the sampler is running once its first line is out
+            while time.time() - t0 < 10 and self.proc.poll() is None and self.path.stat().st_size == 0:
+                time.sleep(0.02)
+            self.start_size = self.path.stat().st_size
         except Exception:
             self.proc = None
         return self
@@ -134,7 +139,9 @@ class ClockSampler:
         if self.proc is None or not self.path.exists():
             return None
         rows = []
-        for line in self.path.read_text().splitlines():
+        text = self.path.read_text()
+        lines = text[getattr(self, "start_size", 0):].splitlines() or text.splitlines()[-1:]
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
                 rows.append(parts)
@@ -187,14 +194,14 @@ def max_over_ranks(x: float, world: int) -> float:
 
 def stage_times(layer, run_step, steps: int) -> list[float]:
     """Average ms per stage over `steps` eager calls, with the library's stage events."""
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(2)]
-    tot = [0.0] * 5
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(2)]
+    tot = [0.0] * 6
     for i in range(steps):
         e = evs[i % 2]
         layer.set_stage_events(e)
         run_step()
         torch.cuda.synchronize()
-        for j in range(5):
+        for j in range(6):
             tot[j] += e[j].elapsed_time(e[j + 1])
     layer.set_stage_events(None)
     return [t / steps for t in tot]
@@ -213,6 +220,13 @@ def run_ours(args):
     B = DECODE_B
     layer = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev, tp_rank=rank, tp_size=world, comm=comm,
                                 max_rows=max(B, PREFILL_B * PREFILL_T if args.prefill else B))
+    if args.only == "prefill":  # profiling case: the prefill workload alone
+        res = run_prefill(args, layer, dev, world, pk, traffic)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "only": "prefill", "prefill": res}), flush=True)
+        if comm is not None:
+            comm.close()
+        return
     g = torch.Generator(device=dev).manual_seed(1)
     s0 = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.1
     hv0 = rank * (HV // world)
@@ -257,9 +271,9 @@ def run_ours(args):
         layer.forward_into(x, out, stream=torch.cuda.current_stream())
 
     st = stage_times(layer, dec_step, min(args.steps, 50))
-    names = ["in_proj", "conv", "recurrence", "out_proj", "allreduce"]
+    names = STAGES
     byt = decode_bytes(B, world)
-    dec_stage = {n: round(t * 1e3, 2) for n, t in zip(names, st) if n != "conv"}
+    dec_stage = {n: round(t * 1e3, 2) for n, t in zip(names, st) if n not in ("conv", "chunk_prep")}
     dom = max(["in_proj", "recurrence", "out_proj"], key=lambda n: dec_stage[n])
     achieved = byt[dom] / (dec_stage[dom] * 1e-6) / 1e9
     tr = traffic.get(f"decode_{dom}")
@@ -341,10 +355,10 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
     barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world) / steps
     st = stage_times(layer_p, lambda: layer_p.forward_into(x, out), min(steps, 3))
-    names = ["in_proj", "conv", "recurrence", "out_proj", "allreduce"]
-    stage = {n: round(t, 3) for n, t in zip(names, st)}
+    stage = {n: round(t, 3) for n, t in zip(STAGES, st)}
     fl = prefill_flops(B, T, world)
     tf = lambda n: fl[n] / (stage[n] * 1e-3) / 1e12
+    rec_ms = stage["chunk_prep"] + stage["recurrence"]
     return {
         "workload": "cfg3: Qwen3.5-9B GDN layer chunked prefill, batch 8 x 8192 tokens, chunk 64",
         "value": round(B * T / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3), "steps": steps,
@@ -355,7 +369,7 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
                      "traffic": traffic.get("prefill_in_proj"), "peak_source": pk["source"] + " (sustained)"},
         "step_tflops": round(fl["step"] / (ms * 1e-3) / 1e12, 1),
         "step_tensor_frac": round(fl["step"] / (ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
-        "recurrence_tflops": round(tf("recurrence"), 2),
+        "recurrence_tflops": round(fl["recurrence"] / (rec_ms * 1e-3) / 1e12, 2),
         "clocks": clk.summary(),
     }
 
@@ -422,7 +436,15 @@ def main():
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--only", choices=["all", "decode", "prefill"], default="all",
+                    help="profiling: run only one workload (the headline line needs 'all')")
+    ap.add_argument("--decode-b", type=int, default=DECODE_B)
+    ap.add_argument("--prefill-b", type=int, default=PREFILL_B)
+    ap.add_argument("--prefill-t", type=int, default=PREFILL_T)
     args = ap.parse_args()
+    globals()["DECODE_B"], globals()["PREFILL_B"], globals()["PREFILL_T"] = args.decode_b, args.prefill_b, args.prefill_t
+    if args.only == "decode":
+        args.prefill = False
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":

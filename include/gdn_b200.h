@@ -114,8 +114,9 @@ GDN_API gdn_status gdn_layer_forward(gdn_layer* layer, const uint16_t* x, int32_
                              float* conv_state, uint16_t* out, gdn_comm* comm, void* stream);
 
 /* Optional stage timing: each forward records events[i] (cudaEvent_t, created by the caller) on its stream:
- * 0 start, 1 after in_proj, 2 after the prefill conv (= 1 for decode), 3 after the recurrence (decode
- * kernel or chunked prefill), 4 after out_proj, 5 after the all-reduce.  count 0 disables.  The reference
+ * 0 start, 1 after in_proj, 2 after the prefill conv, 3 after the chunk preparation (2 and 3 coincide with
+ * 1 for decode), 4 after the recurrence (decode kernel or chunked state pass), 5 after out_proj, 6 after
+ * the all-reduce.  count 0 disables, at most 7.  The reference
  * measures the same per-op split with its device profiler (9B/README.md:137-145). */
 GDN_API gdn_status gdn_layer_set_stage_events(gdn_layer* layer, void* const* events, int32_t count);
 

@@ -1,0 +1,730 @@
+// Chunked (WY/UT) prefill of the gated delta rule on the tcgen05 tensor cores, fused with l2norm, gating
+// and the gated RMSNorm.
+//
+// The reference runs prefill token by token (9B/README.md:150-151,157: chunked prefill "not done yet"); the
+// chunked form is pinned by HF torch_chunk_gated_delta_rule (modeling_qwen3_5.py:234-311) and by the
+// sequential rule (9B/reference.py:28-34).  Per chunk of C = 64 tokens, with in-chunk cumulative log decay
+// G_t, normalised k^, scaled q^ and fp32 state S[d][v]:
+//   M[t][s] = beta_t (k^_t . k^_s) e^(G_t - G_s)  (s < t),   A[t][s] = (q^_t . k^_s) e^(G_t - G_s)  (s <= t)
+//   T  = (I + M)^-1
+//   R  = beta (V - e^G (K^ S))           Vn = T R                     (= U - W S of the WY form)
+//   O  = e^G (Q^ S) + A Vn  -> y = RMSNorm(O) * w * SiLU(z)
+//   S <- e^(G_C) S + (e^(G_C - G) K^)^T Vn
+//
+// Two kernels:
+//   chunk_prep   one CTA per (sequence, k-head, chunk), fully parallel: [K; Q] K^T on the tensor cores,
+//                then per v-head of the GQA group M, A and the fp32 blocked inverse T; T (hi/lo) and A are
+//                written as ready-to-copy 128B-swizzled bf16 tile images.
+//   chunk_state  one CTA per (sequence, v-head), sequential over chunks; the state stays in registers as
+//                S^T (thread v holds a row) and feeds three tcgen05 MMA groups per chunk:
+//                  MMA1  [ (K^S)^T | (e^G Q^ S)^T ] = S^T [K^ ; e^G Q^]^T      (128 x 128, K = 128)
+//                  MMA2  Vn^T = R^T T^T                                        (128 x 64,  K = 64)
+//                  MMA3  dS^T = Vn^T Kd ;  O^T += Vn^T A^T                     (128 x 128 / 128 x 64)
+// Precision: every operand is split into bf16 hi + lo and the products that feed the state use three
+// passes (hi*hi + hi*lo + lo*hi, about 16 mantissa bits); the output-only products use hi*hi.  All tiles are
+// K-major with 128-byte swizzle (64 bf16 per row), the layout the GEMM uses.
+#include <cuda_bf16.h>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace gdn {
+
+namespace {
+
+constexpr int kC = 64;
+constexpr int kD = 128;
+constexpr int kThreads = 256;
+// Per (sequence, v-head, chunk): T hi, T lo, A hi ([64 x 64] bf16 tiles) and the gates (beta, e^G,
+// e^(G_C - G), 64 floats each, plus 64 unused).
+constexpr int kTImageBytes = 3 * 8192 + 1024;
+constexpr int kTGateOff = 3 * 8192;
+// Per (sequence, k-head, chunk), independent of the gates: [k^ ; q^] hi (2 atoms of [128][64]), k^ lo
+// (2 atoms of [64][64]) and k^T hi / lo ([128 d][64 t] each).
+constexpr int kKImageBytes = 32768 + 16384 + 16384 + 16384;
+constexpr int kKOffKQ = 0, kKOffKL = 32768, kKOffKTH = 49152, kKOffKTL = 65536;
+
+// Byte offset of bf16 element (r, k), k < 64, in a K-major tile with 128-byte swizzle (1024-aligned base).
+__device__ __forceinline__ uint32_t sw_off(int r, int k) {
+  return static_cast<uint32_t>(r * 128 + (((k >> 3) ^ (r & 7)) << 4) + ((k & 7) << 1));
+}
+
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+
+// Pack 8 floats into hi and lo uint4 (8 bf16 each).
+__device__ __forceinline__ void pack8(const float* x, uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat16 h0, l0, h1, l1;
+    split_bf16(x[2 * i], h0, l0);
+    split_bf16(x[2 * i + 1], h1, l1);
+    __nv_bfloat162 hh(h0, h1), ll(l0, l1);
+    h[i] = *reinterpret_cast<uint32_t*>(&hh);
+    l[i] = *reinterpret_cast<uint32_t*>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Contiguous global -> shared copy by the TMA engine (no tensor map, no multicast), completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// D (+)= A * B^T over katoms 64-wide K atoms; A and B are K-major SW128 tiles given by the shared address of
+// their first atom and the byte distance between atoms.
+__device__ __forceinline__ void mma_atoms(uint32_t d, uint32_t a, uint32_t a_stride, uint32_t b, uint32_t b_stride,
+                                          int katoms, uint32_t idesc, bool accumulate) {
+  for (int at = 0; at < katoms; ++at) {
+    const uint64_t da = sdesc_k_sw128(a + at * a_stride), db = sdesc_k_sw128(b + at * b_stride);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, (accumulate || at || k) ? 1u : 0u);
+  }
+}
+
+// Per-chunk gating scalars for v-head h: G (inclusive cumsum of g), beta, e^G, e^(G_C - G).  Warp-level.
+__device__ __forceinline__ void chunk_gates(const float* proj, int64_t proj_ld, int64_t a_off, int64_t b_off,
+                                            int64_t row0, int L, int h, float neg_a, float dtb, int lane, float* G,
+                                            float* beta, float* eG, float* eCG) {
+  float g2[2], b2[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = lane + 32 * i;
+    g2[i] = 0.f;
+    b2[i] = 0.f;
+    if (t < L) {
+      const float* pr = proj + (row0 + t) * proj_ld;
+      g2[i] = neg_a * softplus_f(pr[a_off + h] + dtb);
+      b2[i] = sigmoid_f(pr[b_off + h]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, g2[i], off);
+      if (lane >= off) g2[i] += n;
+    }
+  }
+  g2[1] += __shfl_sync(0xffffffffu, g2[0], 31);
+  const float gC = __shfl_sync(0xffffffffu, g2[1], 31);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = lane + 32 * i;
+    G[t] = g2[i];
+    beta[t] = b2[i];
+    if (eG) eG[t] = expf(g2[i]);
+    if (eCG) eCG[t] = expf(gC - g2[i]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------
+// chunk_prep
+// ------------------------------------------------------------------------------------------------------
+constexpr int kLdF = 68;  // padded fp32 row stride of the 64 x 64 work matrices
+
+struct PrepSmem {
+  uint8_t kq_h[2 * 16384];  // [K; Q] hi: 2 atoms of [128 rows][64]
+  uint8_t kq_l[2 * 16384];  // [K; Q] lo
+  float m[kC * kLdF];
+  float t[kC * kLdF];
+  float x[3 * 256];
+  float G[kC], beta[kC], eG[kC], eCG[kC];
+  uint64_t bar;
+  uint32_t tmem;
+};
+
+__global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, uint8_t* kimg, uint8_t* timg,
+                                                                  int nchunks) {
+  extern __shared__ uint8_t smem_raw[];
+  PrepSmem& sm = *reinterpret_cast<PrepSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ch = blockIdx.x % nchunks;
+  const int kh = (blockIdx.x / nchunks) % p.Hk;
+  const int b = blockIdx.x / (nchunks * p.Hk);
+  const int t0 = ch * kC, L = min(kC, p.T - t0);
+  const int64_t row0 = static_cast<int64_t>(b) * p.T + t0;
+  const int kd = p.Hk * kD;
+  const int ratio = p.Hv / p.Hk;
+  const float scale = rsqrtf(static_cast<float>(kD));
+
+  if (tid == 0) {
+    mbar_init(&sm.bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem, 64);
+    tmem_relinquish();
+  }
+  // ---- q^ and k^ rows, split into bf16 hi/lo: rows 0..63 = k, rows 64..127 = q (4 tokens per warp in flight)
+#pragma unroll 1
+  for (int tb = warp; tb < kC; tb += 32) {
+    float4 qv[4], kv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = tb + 8 * u;
+      qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      kv[u] = qv[u];
+      if (t < L) {
+        const float* base = p.qkv + (row0 + t) * p.qkv_ld;
+        qv[u] = reinterpret_cast<const float4*>(base + kh * kD)[lane];
+        kv[u] = reinterpret_cast<const float4*>(base + kd + kh * kD)[lane];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = tb + 8 * u;
+      float sq = qv[u].x * qv[u].x + qv[u].y * qv[u].y + qv[u].z * qv[u].z + qv[u].w * qv[u].w;
+      float sk = kv[u].x * kv[u].x + kv[u].y * kv[u].y + kv[u].z * kv[u].z + kv[u].w * kv[u].w;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        sk += __shfl_xor_sync(0xffffffffu, sk, off);
+      }
+      const float rq = rsqrtf(sq + 1e-6f) * scale, rk = rsqrtf(sk + 1e-6f);
+      const float kvals[4] = {kv[u].x * rk, kv[u].y * rk, kv[u].z * rk, kv[u].w * rk};
+      const float qvals[4] = {qv[u].x * rq, qv[u].y * rq, qv[u].z * rq, qv[u].w * rq};
+      const int d0 = 4 * lane, atom = d0 >> 6, kk = d0 & 63;
+      uint32_t hk[2], lk[2], hq[2], lq[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        __nv_bfloat16 a0, a1, c0, c1;
+        split_bf16(kvals[2 * i], a0, c0);
+        split_bf16(kvals[2 * i + 1], a1, c1);
+        __nv_bfloat162 hh(a0, a1), ll(c0, c1);
+        hk[i] = *reinterpret_cast<uint32_t*>(&hh);
+        lk[i] = *reinterpret_cast<uint32_t*>(&ll);
+        split_bf16(qvals[2 * i], a0, c0);
+        split_bf16(qvals[2 * i + 1], a1, c1);
+        __nv_bfloat162 hq2(a0, a1), lq2(c0, c1);
+        hq[i] = *reinterpret_cast<uint32_t*>(&hq2);
+        lq[i] = *reinterpret_cast<uint32_t*>(&lq2);
+      }
+      *reinterpret_cast<uint2*>(sm.kq_h + atom * 16384 + sw_off(t, kk)) = make_uint2(hk[0], hk[1]);
+      *reinterpret_cast<uint2*>(sm.kq_l + atom * 16384 + sw_off(t, kk)) = make_uint2(lk[0], lk[1]);
+      *reinterpret_cast<uint2*>(sm.kq_h + atom * 16384 + sw_off(64 + t, kk)) = make_uint2(hq[0], hq[1]);
+      *reinterpret_cast<uint2*>(sm.kq_l + atom * 16384 + sw_off(64 + t, kk)) = make_uint2(lq[0], lq[1]);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
+  if (tid == 0) {
+    constexpr uint32_t id = idesc_dense(1, 128, 64);
+    const uint32_t kqh = smem_u32(sm.kq_h), kql = smem_u32(sm.kq_l);
+    mma_atoms(tmem, kqh, 16384, kqh, 16384, 2, id, false);  // [K;Q]h K_h^T
+    mma_atoms(tmem, kqh, 16384, kql, 16384, 2, id, true);   // [K;Q]h K_l^T
+    mma_atoms(tmem, kql, 16384, kqh, 16384, 2, id, true);   // [K;Q]l K_h^T
+    umma_commit(&sm.bar);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&sm.bar, 0, kErrWaitAccum);
+  tc_fence_after();
+  // Row r of the accumulator: r < 64 -> (k_r . k_s), r >= 64 -> (q_(r-64) . k_s); this thread: 32 columns.
+  const int q4 = warp & 3, half = warp >> 2;
+  const int r = q4 * 32 + lane;
+  float acc[32];
+  {
+    float v[16];
+    tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * half, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = v[i];
+    tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * half + 16, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[16 + i] = v[i];
+  }
+  const int s0 = 32 * half;
+  const int t_row = r & 63;
+  const bool is_k = r < 64;
+
+  // ---- the gate-independent operand image of this (sequence, k-head, chunk)
+  {
+    uint8_t* ki = kimg + ((static_cast<int64_t>(b) * p.Hk + kh) * nchunks + ch) * kKImageBytes;
+    const uint4* kq = reinterpret_cast<const uint4*>(sm.kq_h);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) reinterpret_cast<uint4*>(ki + kKOffKQ)[tid + i * kThreads] = kq[tid + i * kThreads];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // k lo: rows 0..63 of both atoms of [K; Q] lo
+      const int idx = tid + i * kThreads, atom = idx >> 9, e = idx & 511;
+      reinterpret_cast<uint4*>(ki + kKOffKL + atom * 8192)[e] = reinterpret_cast<const uint4*>(sm.kq_l + atom * 16384)[e];
+    }
+    // k^T [d][t]: thread (d, half of the tokens) gathers its column from the swizzled row tiles
+    const int d = tid >> 1, th = tid & 1, atom = d >> 6, kk = d & 63;
+    uint16_t hv[32], lv[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t off = atom * 16384 + sw_off(32 * th + j, kk);
+      hv[j] = *reinterpret_cast<const uint16_t*>(sm.kq_h + off);
+      lv[j] = *reinterpret_cast<const uint16_t*>(sm.kq_l + off);
+    }
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) {
+      uint32_t wh[4], wl[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        wh[i] = static_cast<uint32_t>(hv[8 * c8 + 2 * i]) | (static_cast<uint32_t>(hv[8 * c8 + 2 * i + 1]) << 16);
+        wl[i] = static_cast<uint32_t>(lv[8 * c8 + 2 * i]) | (static_cast<uint32_t>(lv[8 * c8 + 2 * i + 1]) << 16);
+      }
+      *reinterpret_cast<uint4*>(ki + kKOffKTH + sw_off(d, 32 * th + 8 * c8)) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+      *reinterpret_cast<uint4*>(ki + kKOffKTL + sw_off(d, 32 * th + 8 * c8)) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+    }
+  }
+
+  for (int j = 0; j < ratio && ok; ++j) {
+    const int h = kh * ratio + j;
+    if (warp == 0)
+      chunk_gates(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, h, -expf(p.a_log[h]), p.dt_bias[h], lane, sm.G,
+                  sm.beta, sm.eG, sm.eCG);
+    __syncthreads();
+    uint8_t* img = timg + ((static_cast<int64_t>(b) * p.Hv + h) * nchunks + ch) * kTImageBytes;
+    if (tid < kC) {
+      float* gi = reinterpret_cast<float*>(img + kTGateOff);
+      gi[tid] = sm.beta[tid];
+      gi[kC + tid] = sm.eG[tid];
+      gi[2 * kC + tid] = sm.eCG[tid];
+    }
+    const float Gt = sm.G[t_row];
+    if (is_k) {
+      const float bt = sm.beta[t_row];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = s0 + i;
+        sm.m[t_row * kLdF + s] = s < t_row ? bt * acc[i] * expf(Gt - sm.G[s]) : 0.f;
+      }
+    } else {
+      float av[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = s0 + i;
+        av[i] = s <= t_row ? acc[i] * expf(Gt - sm.G[s]) : 0.f;
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        uint4 hi, lo;
+        pack8(av + 8 * c8, hi, lo);
+        *reinterpret_cast<uint4*>(img + 16384 + sw_off(t_row, s0 + 8 * c8)) = hi;  // A tile (hi only)
+      }
+    }
+    __syncthreads();
+    // ---- T = (I + M)^-1: 16 x 16 diagonal blocks by forward substitution, then off-diagonal blocks.
+    if (warp < 4) {
+      const int o = warp * 16, jj = lane & 15;
+      if (lane < 16)
+        for (int i = 0; i < 16; ++i) sm.t[(o + i) * kLdF + o + jj] = (i == jj) ? 1.f : 0.f;
+      __syncwarp();
+      for (int i = 1; i < 16; ++i) {
+        float a = 0.f;
+        if (lane < 16 && jj < i)
+          for (int mm = jj; mm < i; ++mm) a += sm.m[(o + i) * kLdF + o + mm] * sm.t[(o + mm) * kLdF + o + jj];
+        __syncwarp();
+        if (lane < 16 && jj < i) sm.t[(o + i) * kLdF + o + jj] = -a;
+        __syncwarp();
+      }
+    } else {
+      for (int idx = tid - 128; idx < 6 * 256; idx += 128) {  // strictly upper blocks of T are zero
+        const int blk = idx >> 8, e = idx & 255;
+        const int ra = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+        const int cb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+        sm.t[(ra * 16 + (e >> 4)) * kLdF + cb * 16 + (e & 15)] = 0.f;
+      }
+    }
+    __syncthreads();
+    for (int d = 1; d < 4; ++d) {
+      const int nb = 4 - d;
+      for (int idx = tid; idx < nb * 256; idx += kThreads) {  // X = sum_{c=b}^{a-1} M_ac T_cb
+        const int bb = idx >> 8, e = idx & 255, i = e >> 4, jj = e & 15, aa = bb + d;
+        float a = 0.f;
+        for (int c = bb; c < aa; ++c)
+#pragma unroll 4
+          for (int mm = 0; mm < 16; ++mm) a += sm.m[(aa * 16 + i) * kLdF + c * 16 + mm] * sm.t[(c * 16 + mm) * kLdF + bb * 16 + jj];
+        sm.x[idx] = a;
+      }
+      __syncthreads();
+      for (int idx = tid; idx < nb * 256; idx += kThreads) {  // T_ab = -T_aa X
+        const int bb = idx >> 8, e = idx & 255, i = e >> 4, jj = e & 15, aa = bb + d;
+        float a = 0.f;
+        for (int mm = 0; mm <= i; ++mm) a += sm.t[(aa * 16 + i) * kLdF + aa * 16 + mm] * sm.x[bb * 256 + mm * 16 + jj];
+        sm.t[(aa * 16 + i) * kLdF + bb * 16 + jj] = -a;
+      }
+      __syncthreads();
+    }
+    // ---- T image: hi at +0, lo at +8192; thread (row, 16-column quarter)
+    {
+      const int tr = tid >> 2, cq = (tid & 3) * 16;
+      float tv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tv[i] = sm.t[tr * kLdF + cq + i];
+#pragma unroll
+      for (int c8 = 0; c8 < 2; ++c8) {
+        uint4 hi, lo;
+        pack8(tv + 8 * c8, hi, lo);
+        *reinterpret_cast<uint4*>(img + sw_off(tr, cq + 8 * c8)) = hi;
+        *reinterpret_cast<uint4*>(img + 8192 + sw_off(tr, cq + 8 * c8)) = lo;
+      }
+    }
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 64);
+}
+
+// ------------------------------------------------------------------------------------------------------
+// chunk_state
+// ------------------------------------------------------------------------------------------------------
+struct StateSmem {
+  uint8_t st_h[32768];   // S^T hi: 2 atoms of [128 v][64 d]
+  uint8_t st_l[32768];   // S^T lo
+  uint8_t kimg[kKImageBytes];  // this chunk's k-head operand image (bulk-copied)
+  uint8_t tmat[3 * 8192];      // this chunk's T hi, T lo, A hi (bulk-copied)
+  uint8_t rv_h[16384];   // R^T hi [128 v][64 t], later (e^(G_C - G) Vn)^T hi
+  uint8_t rv_l[16384];
+  uint8_t vn_h[16384];   // Vn^T hi
+  float gates[2][4 * kC];  // double-buffered beta | e^G | e^(G_C - G)
+  float red[4][kC];
+  uint64_t bar_kq, bar_kt, bar_t, bar_g[2], bar_mma[3];
+  uint32_t tmem;
+  int abort;
+};
+
+constexpr uint32_t kColP1 = 0, kColVn = 128, kColDs = 256, kColAv = 384;
+
+// One halving step of a warp transpose-reduction: entries [0, N) and [N, 2N) are exchanged with lane ^ N;
+// afterwards a[i] (i < N) holds the pair sum for index i + N * ((lane & N) != 0) of the previous level.
+template <int N>
+__device__ __forceinline__ void butterfly_step(float (&a)[32], int lane) {
+  const bool up = (lane & N) != 0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float send = up ? a[i] : a[i + N];
+    const float keep = up ? a[i + N] : a[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, N);
+  }
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, float* out) {
+  float v[16];
+  tmem_ld16(addr, v);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out[i] = v[i];
+  tmem_ld16(addr + 16, v);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out[16 + i] = v[i];
+}
+
+// Write 32 consecutive k values (k0 .. k0+31, k0 a multiple of 32) of row r into a hi/lo tile pair.
+__device__ __forceinline__ void write_row32(uint8_t* hi_tile, uint8_t* lo_tile, int r, int k0, const float* x) {
+#pragma unroll
+  for (int c8 = 0; c8 < 4; ++c8) {
+    uint4 hi, lo;
+    pack8(x + 8 * c8, hi, lo);
+    *reinterpret_cast<uint4*>(hi_tile + sw_off(r, k0 + 8 * c8)) = hi;
+    if (lo_tile) *reinterpret_cast<uint4*>(lo_tile + sw_off(r, k0 + 8 * c8)) = lo;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, const uint8_t* kimg, const uint8_t* timg,
+                                                                  int nchunks) {
+  extern __shared__ uint8_t smem_raw[];
+  StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.x / p.Hv, h = blockIdx.x % p.Hv;
+  const int kh = h / (p.Hv / p.Hk);
+  const int kd = p.Hk * kD;
+  const int q4 = warp & 3, half = warp >> 2;
+  const int v = q4 * 32 + lane;  // accumulator row (TMEM lane) this thread reads
+  const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
+  const uint8_t* kimg_h = kimg + (static_cast<int64_t>(b) * p.Hk + kh) * nchunks * kKImageBytes;
+  const uint8_t* timg_h = timg + (static_cast<int64_t>(b) * p.Hv + h) * nchunks * kTImageBytes;
+
+  // Bulk copies of chunk c's images (issued by thread 0 as soon as the buffers they overwrite are free).
+  // Thread 0 counts the copies it issued per barrier, so that after an error it can wait out the ones
+  // still in flight before the CTA exits.
+  int n_kq = 0, n_kt = 0, n_g[2] = {0, 0};
+  auto load_kq = [&](int c) {  // [k^; q^] hi and k^ lo: needed by MMA1
+    ++n_kq;
+    mbar_arrive_expect_tx(&sm.bar_kq, kKOffKTH);
+    bulk_load(sm.kimg, kimg_h + static_cast<int64_t>(c) * kKImageBytes, kKOffKTH, &sm.bar_kq);
+  };
+  auto load_kt_t = [&](int c) {  // k^T hi/lo (MMA3) and T, A (MMA2, MMA3)
+    ++n_kt;
+    mbar_arrive_expect_tx(&sm.bar_kt, kKImageBytes - kKOffKTH);
+    bulk_load(sm.kimg + kKOffKTH, kimg_h + static_cast<int64_t>(c) * kKImageBytes + kKOffKTH,
+              kKImageBytes - kKOffKTH, &sm.bar_kt);
+    mbar_arrive_expect_tx(&sm.bar_t, 3 * 8192);
+    bulk_load(sm.tmat, timg_h + static_cast<int64_t>(c) * kTImageBytes, 3 * 8192, &sm.bar_t);
+  };
+  auto load_gates = [&](int c) {
+    ++n_g[c & 1];
+    mbar_arrive_expect_tx(&sm.bar_g[c & 1], 3 * kC * 4);
+    bulk_load(sm.gates[c & 1], timg_h + static_cast<int64_t>(c) * kTImageBytes + kTGateOff, 3 * kC * 4,
+              &sm.bar_g[c & 1]);
+  };
+
+  if (tid == 0) {
+    mbar_init(&sm.bar_kq, 1);
+    mbar_init(&sm.bar_kt, 1);
+    mbar_init(&sm.bar_t, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&sm.bar_g[i], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&sm.bar_mma[i], 1);
+    fence_mbar_init();
+    sm.abort = 0;
+    load_kq(0);
+    load_kt_t(0);
+    load_gates(0);
+    if (nchunks > 1) load_gates(1);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem, 512);
+    tmem_relinquish();
+  }
+  // ---- initial state: thread (v, half) holds S^T[v][64 half .. +63] = S[d][v]
+  float* Sg = p.state + (static_cast<int64_t>(b) * p.Hv + h) * kD * kD;
+  float S[64];
+#pragma unroll
+  for (int j = 0; j < 64; ++j) S[j] = Sg[(64 * half + j) * kD + v];
+#pragma unroll
+  for (int c32 = 0; c32 < 2; ++c32)
+    write_row32(sm.st_h + half * 16384, sm.st_l + half * 16384, v, 32 * c32, S + 32 * c32);
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
+  const float* vbase = p.qkv + 2 * kd + h * kD + v;  // v column of this head
+  const float* zbase = p.proj + p.z_off + h * kD + v;
+  const float w_norm = p.norm_w[v];
+
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int t0 = ch * kC, L = min(kC, p.T - t0);
+    const int64_t row0 = static_cast<int64_t>(b) * p.T + t0;
+    const uint32_t par = ch & 1;
+    const float* gt = sm.gates[ch & 1];
+    const float* g_beta = gt;
+    const float* g_eG = gt + kC;
+    const float* g_eCG = gt + 2 * kC;
+    // ---------------- MMA1: [(K^S)^T | (Q^S)^T] = S^T [K^; Q^]^T ----------------
+    if (tid == 0) {
+      if (!mbar_wait(&sm.bar_kq, par, kErrWaitTmaFull)) sm.abort = 1;
+      tc_fence_after();
+      const uint32_t sth = smem_u32(sm.st_h), stl = smem_u32(sm.st_l), kq = smem_u32(sm.kimg + kKOffKQ);
+      const uint32_t kl = smem_u32(sm.kimg + kKOffKL);
+      mma_atoms(tmem + kColP1, sth, 16384, kq, 16384, 2, idesc_dense(1, 128, 128), false);
+      mma_atoms(tmem + kColP1, stl, 16384, kq, 16384, 2, idesc_dense(1, 128, 128), true);
+      mma_atoms(tmem + kColP1, sth, 16384, kl, 8192, 2, idesc_dense(1, 128, 64), true);
+      umma_commit(&sm.bar_mma[0]);
+    }
+    // V for phase R, in flight during MMA1
+    float vt[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = 32 * half + j;
+      vt[j] = t < L ? vbase[(row0 + t) * p.qkv_ld] : 0.f;
+    }
+    __syncwarp();
+    if (!mbar_wait(&sm.bar_g[ch & 1], (ch >> 1) & 1, kErrWaitTmaFull)) sm.abort = 1;
+    if (!mbar_wait(&sm.bar_mma[0], par, kErrWaitAccum)) sm.abort = 1;
+    tc_fence_after();
+    if (tid == 0 && ch + 1 < nchunks) load_kq(ch + 1);  // MMA1 has consumed [K; Q] and k lo
+    // ---------------- phase R: R^T[v][t] = beta_t (V[t][v] - e^G_t (K^S)^T[v][t]) ----------------
+    {
+      float ks[32];
+      tmem_ld32(tmem + lane_base + kColP1 + 32 * half, ks);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int t = 32 * half + j;
+        ks[j] = g_beta[t] * (vt[j] - g_eG[t] * ks[j]);
+      }
+      write_row32(sm.rv_h, sm.rv_l, v, 32 * half, ks);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (sm.abort) break;
+    // ---------------- MMA2: Vn^T = R^T T^T ----------------
+    if (tid == 0) {
+      if (!mbar_wait(&sm.bar_t, par, kErrWaitTmaFull)) sm.abort = 1;
+      tc_fence_after();
+      const uint32_t rh = smem_u32(sm.rv_h), rl = smem_u32(sm.rv_l), th = smem_u32(sm.tmat), tl = smem_u32(sm.tmat + 8192);
+      constexpr uint32_t id = idesc_dense(1, 128, 64);
+      mma_atoms(tmem + kColVn, rh, 0, th, 0, 1, id, false);
+      mma_atoms(tmem + kColVn, rl, 0, th, 0, 1, id, true);
+      mma_atoms(tmem + kColVn, rh, 0, tl, 0, 1, id, true);
+      umma_commit(&sm.bar_mma[1]);
+    }
+    __syncwarp();
+    if (!mbar_wait(&sm.bar_mma[1], par, kErrWaitAccum)) sm.abort = 1;
+    tc_fence_after();
+    // ---------------- phase V: Vn^T hi (for A Vn) and (e^(G_C - G) Vn)^T hi/lo (for the state) ----------------
+    {
+      float vn[32];
+      tmem_ld32(tmem + lane_base + kColVn + 32 * half, vn);
+      write_row32(sm.vn_h, nullptr, v, 32 * half, vn);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) vn[j] *= g_eCG[32 * half + j];
+      write_row32(sm.rv_h, sm.rv_l, v, 32 * half, vn);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (sm.abort) break;
+    // ---------------- MMA3: dS^T = (e^(G_C-G) Vn)^T K^ ; (A Vn)^T = Vn^T A^T ----------------
+    if (tid == 0) {
+      if (!mbar_wait(&sm.bar_kt, par, kErrWaitTmaFull)) sm.abort = 1;
+      tc_fence_after();
+      const uint32_t rh = smem_u32(sm.rv_h), rl = smem_u32(sm.rv_l);
+      const uint32_t kth = smem_u32(sm.kimg + kKOffKTH), ktl = smem_u32(sm.kimg + kKOffKTL);
+      constexpr uint32_t id128 = idesc_dense(1, 128, 128), id64 = idesc_dense(1, 128, 64);
+      mma_atoms(tmem + kColDs, rh, 0, kth, 0, 1, id128, false);
+      mma_atoms(tmem + kColDs, rl, 0, kth, 0, 1, id128, true);
+      mma_atoms(tmem + kColDs, rh, 0, ktl, 0, 1, id128, true);
+      mma_atoms(tmem + kColAv, smem_u32(sm.vn_h), 0, smem_u32(sm.tmat + 16384), 0, 1, id64, false);
+      umma_commit(&sm.bar_mma[2]);
+    }
+    // z for the output, in flight during MMA3
+    float zt[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = 32 * half + j;
+      zt[j] = t < L ? zbase[(row0 + t) * p.proj_ld] : 0.f;
+    }
+    __syncwarp();
+    if (!mbar_wait(&sm.bar_mma[2], par, kErrWaitAccum)) sm.abort = 1;
+    tc_fence_after();
+    if (tid == 0 && ch + 1 < nchunks) load_kt_t(ch + 1);  // k^T, T and A have been consumed
+    // ---------------- output: O^T[v][t] = e^G_t (Q^S)^T + (A Vn)^T -> RMSNorm over v -> y ----------------
+    float o[32];
+    {
+      float av[32];
+      tmem_ld32(tmem + lane_base + kColP1 + 64 + 32 * half, o);
+      tmem_ld32(tmem + lane_base + kColAv + 32 * half, av);
+      float a[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        o[j] = g_eG[32 * half + j] * o[j] + av[j];
+        a[j] = o[j] * o[j];
+      }
+      // Butterfly: after the 5 steps lane l holds the warp's sum for t index 32 half + l.
+      butterfly_step<16>(a, lane);
+      butterfly_step<8>(a, lane);
+      butterfly_step<4>(a, lane);
+      butterfly_step<2>(a, lane);
+      butterfly_step<1>(a, lane);
+      sm.red[q4][32 * half + lane] = a[0];
+    }
+    // ---------------- state: S^T <- e^(G_C) S^T + dS^T ----------------
+    {
+      const float eC = g_eG[kC - 1];
+#pragma unroll
+      for (int c32 = 0; c32 < 2; ++c32) {
+        float ds[32];
+        tmem_ld32(tmem + lane_base + kColDs + 64 * half + 32 * c32, ds);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) S[32 * c32 + j] = eC * S[32 * c32 + j] + ds[j];
+      }
+#pragma unroll
+      for (int c32 = 0; c32 < 2; ++c32)
+        write_row32(sm.st_h + half * 16384, sm.st_l + half * 16384, v, 32 * c32, S + 32 * c32);
+    }
+    __syncthreads();  // red[] complete
+    {
+      __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(p.y) + static_cast<int64_t>(h) * kD + v;
+      const int64_t y_ld = static_cast<int64_t>(p.Hv) * kD;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int t = 32 * half + j;
+        if (t < L) {
+          const float ms = (sm.red[0][t] + sm.red[1][t] + sm.red[2][t] + sm.red[3][t]) * (1.0f / kD);
+          yb[(row0 + t) * y_ld] = __float2bfloat16_rn(o[j] * rsqrtf(ms + p.eps) * w_norm * silu_f(zt[j]));
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && ch + 2 < nchunks) load_gates(ch + 2);  // this chunk's gate buffer is free again
+    if (sm.abort) break;
+  }
+#pragma unroll
+  for (int j = 0; j < 64; ++j) Sg[(64 * half + j) * kD + v] = S[j];
+  // After an error the loop may end with bulk copies still in flight into this CTA's shared memory: wait
+  // (bounded) for the last phase of every barrier with an issued copy before the CTA exits.  Phase k of a
+  // barrier has parity k & 1; waiting on an already completed phase returns at once.
+  if (tid == 0 && sm.abort) {
+    if (n_kq) mbar_wait(&sm.bar_kq, (n_kq - 1) & 1, kErrWaitTmaFull);
+    if (n_kt) {
+      mbar_wait(&sm.bar_kt, (n_kt - 1) & 1, kErrWaitTmaFull);
+      mbar_wait(&sm.bar_t, (n_kt - 1) & 1, kErrWaitTmaFull);
+    }
+    for (int i = 0; i < 2; ++i)
+      if (n_g[i]) mbar_wait(&sm.bar_g[i], (n_g[i] - 1) & 1, kErrWaitTmaFull);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace
+
+size_t chunk_prefill_scratch_bytes(int B, int T, int Hk, int Hv) {
+  const int64_t nchunks = (T + kC - 1) / kC;
+  return static_cast<size_t>(B) * nchunks * (static_cast<size_t>(Hk) * kKImageBytes + static_cast<size_t>(Hv) * kTImageBytes);
+}
+
+static cudaError_t check_chunk_args(const ChunkArgs& a, const void* scratch) {
+  if (a.B <= 0 || a.T <= 0 || a.Hk <= 0 || a.Hv <= 0 || a.Hv % a.Hk) return cudaErrorInvalidValue;
+  if ((a.qkv_ld & 3) || (reinterpret_cast<uintptr_t>(scratch) & 15)) return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+// Scratch layout: all k-head images, then all v-head images.
+static void split_scratch(const ChunkArgs& a, const void* scratch, uint8_t** kimg, uint8_t** timg) {
+  const int64_t nchunks = (a.T + kC - 1) / kC;
+  *kimg = static_cast<uint8_t*>(const_cast<void*>(scratch));
+  *timg = *kimg + static_cast<int64_t>(a.B) * a.Hk * nchunks * kKImageBytes;
+}
+
+cudaError_t chunk_prep(const ChunkArgs& a, void* scratch, cudaStream_t stream) {
+  cudaError_t e = check_chunk_args(a, scratch);
+  if (e != cudaSuccess) return e;
+  const int nchunks = (a.T + kC - 1) / kC;
+  const int smem = static_cast<int>(sizeof(PrepSmem)) + 1024;
+  e = cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  uint8_t *kimg, *timg;
+  split_scratch(a, scratch, &kimg, &timg);
+  count_launch();
+  chunk_prep_kernel<<<a.B * a.Hk * nchunks, kThreads, smem, stream>>>(a, kimg, timg, nchunks);
+  return cudaGetLastError();
+}
+
+cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t stream) {
+  cudaError_t e = check_chunk_args(a, scratch);
+  if (e != cudaSuccess) return e;
+  const int nchunks = (a.T + kC - 1) / kC;
+  const int smem = static_cast<int>(sizeof(StateSmem)) + 1024;
+  e = cudaFuncSetAttribute(chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  uint8_t *kimg, *timg;
+  split_scratch(a, scratch, &kimg, &timg);
+  count_launch();
+  chunk_state_kernel<<<a.B * a.Hv, kThreads, smem, stream>>>(a, kimg, timg, nchunks);
+  return cudaGetLastError();
+}
+
+}  // namespace gdn

@@ -100,19 +100,21 @@ struct gdn_layer {
   float* norm_w = nullptr;          // [128]
   void* ws = nullptr;
   size_t ws_bytes = 0;
-  cudaEvent_t stage_events[6] = {};  // optional stage timing (gdn_layer_set_stage_events)
+  cudaEvent_t stage_events[7] = {};  // optional stage timing (gdn_layer_set_stage_events)
   int n_stage_events = 0;
 };
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// Workspace layout for n token rows: proj fp32 [n, proj_ld] | qkv fp32 [n, conv_dim] | y bf16 [n, vd]
-static size_t workspace_bytes(const gdn_layer* L, int64_t n) {
-  return align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4) + align256(n * L->vd * 2);
+// Workspace layout for n token rows in `chunks` (sequence, chunk) pairs:
+//   proj fp32 [n, proj_ld] | qkv fp32 [n, conv_dim] | y bf16 [n, vd] | chunk tile images
+static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks) {
+  return align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4) + align256(n * L->vd * 2) +
+         align256(chunk_prefill_scratch_bytes(1, 64, L->hk, L->hv) * static_cast<size_t>(chunks));
 }
 
-static gdn_status ensure_workspace(gdn_layer* L, int64_t n, cudaStream_t stream) {
-  const size_t need = workspace_bytes(L, n);
+static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream) {
+  const size_t need = workspace_bytes(L, n, chunks);
   if (need <= L->ws_bytes) return GDN_OK;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
@@ -250,7 +252,8 @@ extern "C" gdn_status gdn_layer_get_info(const gdn_layer* L, gdn_layer_info* inf
 extern "C" gdn_status gdn_layer_reserve(gdn_layer* L, int64_t max_tokens) {
   if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_reserve: null layer");
   if (max_tokens <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens must be > 0");
-  return ensure_workspace(L, max_tokens, nullptr);
+  // prefill chunks: B * ceil(T / 64) <= max_tokens / 64 + B; room for up to 64 ragged sequences
+  return ensure_workspace(L, max_tokens, max_tokens / 64 + 64, nullptr);
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -261,9 +264,9 @@ static cudaError_t stage_mark(const gdn_layer* L, int i, cudaStream_t s) {
 
 extern "C" gdn_status gdn_layer_set_stage_events(gdn_layer* L, void* const* events, int32_t count) {
   if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_set_stage_events: null layer");
-  if (count < 0 || count > 6 || (count > 0 && !events))
+  if (count < 0 || count > 7 || (count > 0 && !events))
     return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_layer_set_stage_events: count %d", count);
-  for (int i = 0; i < 6; ++i) L->stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  for (int i = 0; i < 7; ++i) L->stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
   L->n_stage_events = count;
   return GDN_OK;
 }
@@ -281,13 +284,15 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   }
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const int64_t n = static_cast<int64_t>(B) * T;
-  gdn_status st = ensure_workspace(L, n, stream);
+  const int64_t chunks = T > 1 ? static_cast<int64_t>(B) * ((T + 63) / 64) : 0;
+  gdn_status st = ensure_workspace(L, n, chunks, stream);
   if (st != GDN_OK) return st;
   const int h = L->dims.hidden;
   char* ws = static_cast<char*>(L->ws);
   float* proj = reinterpret_cast<float*>(ws);
   float* qkv = reinterpret_cast<float*>(ws + align256(n * L->proj_ld * 4));
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4));
+  void* chunk_scratch = ws + align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4) + align256(n * L->vd * 2);
   const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
 
   GDN_CUDA(stage_mark(L, 0, stream));
@@ -303,9 +308,10 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     ep.conv_state = conv_state;
     ep.a_log = L->a_log;
     ep.dt_bias = L->dt_bias;
-    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream));
+    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
     GDN_CUDA(stage_mark(L, 1, stream));
     GDN_CUDA(stage_mark(L, 2, stream));
+    GDN_CUDA(stage_mark(L, 3, stream));
     RecurrenceArgs ra;
     ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
     ra.k = proj + L->kd; ra.k_tok = L->proj_ld; ra.k_head = kHeadDim;
@@ -320,19 +326,19 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     ra.B = B; ra.T = 1; ra.Hk = L->hk; ra.Hv = L->hv;
     ra.scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
     ra.l2norm = 1;
-    GDN_CUDA(recurrence_forward(ra, stream));
-    GDN_CUDA(stage_mark(L, 3, stream));
+    GDN_CUDA(recurrence_forward(ra, stream, true));
+    GDN_CUDA(stage_mark(L, 4, stream));
     GemmEpiArgs eo;
     eo.out = out;
     eo.ld = h;
-    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream));
-    GDN_CUDA(stage_mark(L, 4, stream));
+    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
+    GDN_CUDA(stage_mark(L, 5, stream));
   } else {
     // ---- prefill: in_proj -> conv -> chunked recurrence + gated RMSNorm -> out_proj
     GemmEpiArgs ep;
     ep.out = proj;
     ep.ld = L->proj_ld;
-    GDN_CUDA(gemm_bf16_tn(x, h, L->w_in, h, static_cast<int>(n), L->rows, h, kEpiStoreF32, ep, 1, stream));
+    GDN_CUDA(gemm_bf16_tn(x, h, L->w_in, h, static_cast<int>(n), L->rows, h, kEpiStoreF32, ep, 1, stream, true));
     GDN_CUDA(stage_mark(L, 1, stream));
     GDN_CUDA(conv_prefill(proj, L->proj_ld, qkv, L->conv_dim, L->conv_w, conv_state, B, T, L->conv_dim, stream));
     GDN_CUDA(stage_mark(L, 2, stream));
@@ -343,13 +349,15 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     ca.a_log = L->a_log; ca.dt_bias = L->dt_bias; ca.norm_w = L->norm_w; ca.eps = L->dims.eps;
     ca.state = rec_state; ca.y = y;
     ca.B = B; ca.T = T; ca.Hk = L->hk; ca.Hv = L->hv;
-    GDN_CUDA(chunk_prefill(ca, stream));
+    GDN_CUDA(chunk_prep(ca, chunk_scratch, stream));
     GDN_CUDA(stage_mark(L, 3, stream));
+    GDN_CUDA(chunk_state(ca, chunk_scratch, stream));
+    GDN_CUDA(stage_mark(L, 4, stream));
     GemmEpiArgs eo;
     eo.out = out;
     eo.ld = h;
-    GDN_CUDA(gemm_bf16_tn(y, L->vd, L->w_out, L->vd, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, 1, stream));
-    GDN_CUDA(stage_mark(L, 4, stream));
+    GDN_CUDA(gemm_bf16_tn(y, L->vd, L->w_out, L->vd, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, 1, stream, true));
+    GDN_CUDA(stage_mark(L, 5, stream));
   }
   if (L->tp_size > 1 && comm) {
     const NcclApi& api = nccl();
@@ -357,7 +365,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     ncclResult_t r = api.allReduce(out, out, static_cast<size_t>(n) * h, ncclBfloat16, ncclSum, comm->comm, stream);
     if (r != ncclSuccess) return fail(GDN_ERR_NCCL, "ncclAllReduce: %s", api.getErrorString(r));
   }
-  GDN_CUDA(stage_mark(L, 5, stream));
+  GDN_CUDA(stage_mark(L, 6, stream));
   return GDN_OK;
 }
 

@@ -3,8 +3,9 @@
 //   warp 0      TMA producer (one elected lane), STAGES-deep ring of 128B-swizzled A/B tiles
 //   warp 1      TMEM allocator and UMMA issuer (one elected lane), commits free stages back to warp 0
 //   warps 2..5  epilogue: tcgen05.ld of the 32-lane TMEM quarter (warp % 4) -> fused epilogue -> global
-// Split-K (skinny decode GEMMs) runs the K-slices of a tile as one thread-block cluster; the slices'
-// fp32 partial tiles are summed by the leader CTA through distributed shared memory.
+// Split-K (skinny decode GEMMs) runs the K-slices of a tile as one thread-block cluster; each slice parks
+// its fp32 partial tile in shared memory and then sums a share of the tile's column chunks over all slices
+// through distributed shared memory, so the reduction and the epilogue are spread over the cluster.
 //
 // The two GEMMs of the layer use it as:
 //   in_proj  (9B/gdn_layer.py:255-259: ttnn.linear for qkv+z and for a,b) fused into ONE weight
@@ -92,18 +93,27 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
     const int cr = ep.conv_rows;
     if (m < cr) {
       // Causal conv over the last 3 inputs (conv_state rows 0..2, oldest first) and this token; the
-      // state rolls by one (9B/kernels/layer_reader.cpp:184-197; HF torch_causal_conv1d_update).
+      // state rolls by one (9B/kernels/layer_reader.cpp:184-197; HF torch_causal_conv1d_update).  All 48
+      // history loads are issued before any store so their latencies overlap.
       const float4 w = *reinterpret_cast<const float4*>(ep.conv_w + static_cast<int64_t>(m) * 4);
+      float h0[16], h1[16], h2[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + j;
+        const float* cs = ep.conv_state + static_cast<int64_t>(n < N ? n : 0) * 3 * cr + m;
+        h0[j] = cs[0];
+        h1[j] = cs[cr];
+        h2[j] = cs[2 * cr];
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int n = n0 + j;
         if (n < N) {
           float* cs = ep.conv_state + static_cast<int64_t>(n) * 3 * cr + m;
-          const float s0 = cs[0], s1 = cs[cr], s2 = cs[2 * cr], x = v[j];
-          cs[0] = s1;
-          cs[cr] = s2;
-          cs[2 * cr] = x;
-          out[static_cast<int64_t>(n) * ep.ld + m] = silu_f(w.x * s0 + w.y * s1 + w.z * s2 + w.w * x);
+          cs[0] = h1[j];
+          cs[cr] = h2[j];
+          cs[2 * cr] = v[j];
+          out[static_cast<int64_t>(n) * ep.ld + m] = silu_f(w.x * h0[j] + w.y * h1[j] + w.z * h2[j] + w.w * v[j]);
         }
       }
     } else if (m < cr + ep.z_rows) {
@@ -129,7 +139,7 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, int ksplit, int n_tiles, int group_m, GemmEpiArgs ep) {
+                   int K, int ksplit, int n_tiles, int group_m, int trigger_early, GemmEpiArgs ep) {
   using C = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -173,6 +183,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (trigger_early) griddep_launch_dependents();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -180,9 +191,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool a_streamed = EPI == kEpiStoreF32T || EPI == kEpiStoreBF16T || EPI == kEpiDecodeInProj;
       const uint64_t pol_a = a_streamed ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = policy_evict_last();
-      for (int i = 0; i < nk; ++i) {
+      // The weight operand (A for the transposed decode epilogues, B otherwise) does not depend on the
+      // previous kernel: its first stages are requested before waiting for that kernel to finish.
+      const int pre = nk < STAGES ? nk : STAGES;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+        const int kx = (kb0 + i) * kBK;
+        if (a_streamed) tma_load_2d(sA + i * C::kABytes, &tmA, &full[i], kx, m_tile * kBM, pol_a);
+        else tma_load_2d(sB + i * C::kBBytes, &tmB, &full[i], kx, n_tile * BN, pol_b);
+      }
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) {
+        const int kx = (kb0 + i) * kBK;
+        if (a_streamed) tma_load_2d(sB + i * C::kBBytes, &tmB, &full[i], kx, n_tile * BN, pol_b);
+        else tma_load_2d(sA + i * C::kABytes, &tmA, &full[i], kx, m_tile * kBM, pol_a);
+      }
+      for (int i = pre; i < nk; ++i) {
         const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, kErrWaitSmemEmpty)) break;
+        if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, kErrWaitSmemEmpty)) break;
         mbar_arrive_expect_tx(&full[s], C::kStageBytes);
         const int kx = (kb0 + i) * kBK;
         tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kx, m_tile * kBM, pol_a);
@@ -214,13 +240,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
   const bool epi_warp = warp >= 2;
   if (epi_warp) {
+    griddep_wait();  // the epilogue writes buffers the previous kernel may still read
     mbar_wait(accum, 0, kErrWaitAccum);
     tc_fence_after();
   }
-  if (ksplit > 1) {
-    if (epi_warp && split != 0) {
-      // Non-leader slices park their partial tile in their own (now idle) stage ring.
-      float4* part = reinterpret_cast<float4*>(smem);
+  if (ksplit == 1) {
+    if (epi_warp) {
+      const int m = m_tile * kBM + r;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(t_row + c0, v);
+        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
+      }
+    }
+  } else {
+    // Split-K over the cluster: every slice parks its fp32 partial tile in its own (now idle) stage ring,
+    // then slice s sums 16-column chunks s, s + ksplit, ... over all slices through distributed shared
+    // memory and runs the epilogue for them, so the reduction and the epilogue are spread over the cluster.
+    float4* part = reinterpret_cast<float4*>(smem);
+    if (epi_warp) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
@@ -232,32 +271,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
     cluster_sync();
-  }
-  if (epi_warp && split == 0) {
-    const int m = m_tile * kBM + r;
-    const uint32_t part_addr = smem_u32(smem);
+    if (epi_warp) {
+      const int m = m_tile * kBM + r;
+      const uint32_t part_addr = smem_u32(smem);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      tmem_ld16(t_row + c0, v);
-#pragma unroll 1
-      for (int rank = 1; rank < ksplit; ++rank) {
-        const uint32_t base = mapa_shared(part_addr, rank);
+      for (int c0 = split * 16; c0 < BN; c0 += 16 * ksplit) {
+        float v[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 p = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
-          v[4 * i] += p.x;
-          v[4 * i + 1] += p.y;
-          v[4 * i + 2] += p.z;
-          v[4 * i + 3] += p.w;
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+#pragma unroll
+        for (int rank = 0; rank < 8; ++rank) {
+          if (rank < ksplit) {
+            const uint32_t base = mapa_shared(part_addr, rank);
+            float4 p4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p4[i] = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              v[4 * i] += p4[i].x;
+              v[4 * i + 1] += p4[i].y;
+              v[4 * i + 2] += p4[i].z;
+              v[4 * i + 3] += p4[i].w;
+            }
+          }
         }
+        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
       }
-      epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
     }
-  }
-  if (ksplit > 1) {
     __syncwarp();
-    cluster_sync();  // peers keep their shared memory until the leader has read it
+    cluster_sync();  // every slice keeps its shared memory until all have read it
   }
   tc_fence_before();
   __syncthreads();
@@ -298,73 +340,106 @@ static cudaError_t make_tmap(CUtensorMap* map, const void* ptr, int64_t rows, in
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int BN, int STAGES, int EPI>
-static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit,
-                               const GemmEpiArgs& ep, cudaStream_t stream) {
-  using C = GemmCfg<BN, STAGES>;
-  auto kern = gemm_tn_kernel<BN, STAGES, EPI>;
-  static bool attr_set = false;  // per instantiation; the attribute is per-device-context but idempotent
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-  if (e != cudaSuccess) return e;
-  attr_set = true;
-  (void)attr_set;
-  const int m_tiles = (M + kBM - 1) / kBM;
-  const int n_tiles = (N + BN - 1) / BN;
-  const int tiles = m_tiles * n_tiles;
-  const int group_m = std::min(16, m_tiles);
+// How many clusters of `ks` CTAs of this kernel can be resident at once (the unit a split-K launch is
+// scheduled in: a cluster must fit inside one GPC, so CTA-level occupancy overestimates it).
+template <class Kern>
+static int cluster_capacity(Kern kern, int ks, int smem) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * ksplit));
+  cfg.gridDim = dim3(static_cast<unsigned>(ks * 64));
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
-  cfg.stream = stream;
+  cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(ksplit);
+  attr[0].val.clusterDim.x = static_cast<unsigned>(ks);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = ksplit > 1 ? 1 : 0;
-  count_launch();
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, n_tiles, group_m, ep);
-}
-
-template <int BN, int STAGES>
-static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                                int ksplit, const GemmEpiArgs& ep, cudaStream_t s) {
-  switch (epi) {
-    case kEpiStoreF32: return launch_gemm<BN, STAGES, kEpiStoreF32>(ta, tb, M, N, K, ksplit, ep, s);
-    case kEpiStoreBF16: return launch_gemm<BN, STAGES, kEpiStoreBF16>(ta, tb, M, N, K, ksplit, ep, s);
-    case kEpiStoreF32T: return launch_gemm<BN, STAGES, kEpiStoreF32T>(ta, tb, M, N, K, ksplit, ep, s);
-    case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T>(ta, tb, M, N, K, ksplit, ep, s);
-    case kEpiDecodeInProj: return launch_gemm<BN, STAGES, kEpiDecodeInProj>(ta, tb, M, N, K, ksplit, ep, s);
-    default: return cudaErrorInvalidValue;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    int blocks = 0, dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, kGemmThreads, smem);
+    n = std::max(1, blocks * sms / ks);
   }
+  return n;
 }
 
-static int pick_ksplit(int tiles, int kblocks, int num_sms) {
-  if (tiles >= num_sms) return 1;
+// Split-K factor that minimises (waves of clusters) x (k-blocks per slice), from the real cluster
+// occupancy; ties go to the smaller split.
+template <class Kern>
+static int choose_ksplit(Kern kern, int smem, int tiles, int kblocks) {
+  static int cap[9] = {0};  // per kernel instantiation, filled on first use
   int best = 1;
-  double best_eff = 0.0;
+  double best_cost = 1e30;
   for (int ks = 1; ks <= 8 && ks <= kblocks; ++ks) {
-    const int ctas = tiles * ks;
-    const int waves = (ctas + num_sms - 1) / num_sms;
-    const double eff = static_cast<double>(ctas) / (static_cast<double>(waves) * num_sms);
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
+    if (!cap[ks]) cap[ks] = cluster_capacity(kern, ks, smem);
+    const double waves = static_cast<double>((tiles + cap[ks] - 1) / cap[ks]);
+    const double cost = waves * ((kblocks + ks - 1) / ks) + (ks > 1 ? 2.0 : 0.0);  // + reduction overhead
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
       best = ks;
     }
   }
   return best;
 }
 
-static int sm_count() {
-  int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n;
+template <int BN, int STAGES, int EPI>
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit,
+                               const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t stream) {
+  using C = GemmCfg<BN, STAGES>;
+  auto kern = gemm_tn_kernel<BN, STAGES, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
+  const int kblocks = (K + kBK - 1) / kBK;
+  if (ksplit <= 0) ksplit = choose_ksplit(kern, C::kSmemBytes, tiles, kblocks);
+  ksplit = std::max(1, std::min(ksplit, std::min(8, kblocks)));
+  const int group_m = std::min(16, m_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * ksplit));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (ksplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = static_cast<unsigned>(ksplit);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, n_tiles, group_m, trigger ? 1 : 0, ep);
+}
+
+template <int BN, int STAGES>
+static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                                int ksplit, const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t s) {
+  switch (epi) {
+    case kEpiStoreF32: return launch_gemm<BN, STAGES, kEpiStoreF32>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiStoreBF16: return launch_gemm<BN, STAGES, kEpiStoreBF16>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiStoreF32T: return launch_gemm<BN, STAGES, kEpiStoreF32T>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiDecodeInProj: return launch_gemm<BN, STAGES, kEpiDecodeInProj>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
-                         const GemmEpiArgs& ep, int ksplit, cudaStream_t stream) {
+                         const GemmEpiArgs& ep, int ksplit, cudaStream_t stream, bool pdl, bool trigger) {
   if (M <= 0 || N <= 0 || K <= 0 || (K & 7)) return cudaErrorInvalidValue;
   int BN;
   if (N <= 16) BN = 16;
@@ -377,16 +452,14 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   if (e != cudaSuccess) return e;
   e = make_tmap(&tb, B, N, K, ldb, BN);
   if (e != cudaSuccess) return e;
-  const int kblocks = (K + kBK - 1) / kBK;
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  if (ksplit <= 0) ksplit = pick_ksplit(tiles, kblocks, sm_count());
-  ksplit = std::max(1, std::min(ksplit, std::min(8, kblocks)));
+  // Skinny (decode) tiles use a 3-stage ring (< 75 KB) so three CTAs share an SM and a split-K launch fits
+  // in one wave of clusters; wide tiles take the whole SM.
   switch (BN) {
-    case 16: return dispatch_epi<16, 8>(epi, ta, tb, M, N, K, ksplit, ep, stream);
-    case 32: return dispatch_epi<32, 8>(epi, ta, tb, M, N, K, ksplit, ep, stream);
-    case 64: return dispatch_epi<64, 8>(epi, ta, tb, M, N, K, ksplit, ep, stream);
-    case 128: return dispatch_epi<128, 6>(epi, ta, tb, M, N, K, ksplit, ep, stream);
-    default: return dispatch_epi<256, 4>(epi, ta, tb, M, N, K, ksplit, ep, stream);
+    case 16: return dispatch_epi<16, 3>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    case 32: return dispatch_epi<32, 3>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    case 64: return dispatch_epi<64, 3>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    case 128: return dispatch_epi<128, 6>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    default: return dispatch_epi<256, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
   }
 }
 

@@ -35,8 +35,15 @@ struct GemmEpiArgs {
 // A: [M, K] bf16 row-major with row stride lda (elements); B: [N, K] bf16 row-major with row stride ldb.
 // ksplit > 1 splits K over a cluster of ksplit CTAs whose partial tiles are summed through
 // distributed shared memory (no global workspace).  ksplit = 0 picks a value.
+// pdl: launch with programmatic stream serialization (the kernel may start while the previous kernel in
+// the stream is still running; it prefetches the weight operand -- A for the transposed epilogues, B
+// otherwise -- and waits for the previous kernel before touching anything else).
+// trigger: let the next programmatically serialized kernel start as soon as every CTA of this one runs.
+// Only a kernel whose successor reads nothing that an earlier, still running kernel may write can set it;
+// the last kernel of a layer call never does, so consecutive calls stay ordered.
 cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
-                         const GemmEpiArgs& args, int ksplit, cudaStream_t stream);
+                         const GemmEpiArgs& args, int ksplit, cudaStream_t stream, bool pdl = false,
+                         bool trigger = false);
 
 // Number of kernel launches issued by this library since load (for the benchmark's launch count).
 uint64_t launch_count();

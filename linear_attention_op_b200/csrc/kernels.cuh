@@ -38,7 +38,8 @@ struct RecurrenceArgs {
 };
 
 // Token-by-token gated delta rule, one CTA per (sequence, v-head), state kept in registers.
-cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream);
+// pdl: may start while the previous kernel (the in_proj GEMM) runs; it loads the state first.
+cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream, bool pdl = false);
 
 // Prefill causal conv (K = 4) + SiLU: in[row * in_ld + c] pre-conv channels c < C, out[row * out_ld + c].
 // conv_state [B, 3, C] supplies the history before t = 0 and is then rolled to the last 3 inputs.
@@ -51,7 +52,7 @@ struct ChunkArgs {
   int64_t qkv_ld = 0;
   const float* proj = nullptr;  // in_proj output rows [B*T, proj_ld]: z at z_off, a at a_off, b at b_off
   int64_t proj_ld = 0;
-  int64_t z_off = 0, a_off = 0, b_off = 0;
+  int64_t z_off = 0, a_off = 0, b_off = 0;  // column offsets of z, a and b inside a proj row
   const float* a_log = nullptr;
   const float* dt_bias = nullptr;
   const float* norm_w = nullptr;
@@ -60,6 +61,12 @@ struct ChunkArgs {
   void* y = nullptr;       // bf16 [B*T, Hv*128]
   int B = 0, T = 0, Hk = 0, Hv = 0;
 };
-cudaError_t chunk_prefill(const ChunkArgs& a, cudaStream_t stream);
+// Scratch (bytes) the chunked prefill needs for B sequences of T tokens: per (sequence, k-head, chunk) the
+// bf16 operand tiles of k^ and q^ (80 KB), per (sequence, v-head, chunk) the tiles of T and A and the gates
+// (25 KB).
+size_t chunk_prefill_scratch_bytes(int B, int T, int Hk, int Hv);
+// chunk_prep writes the tile images into scratch; chunk_state (stream-ordered after it) consumes them.
+cudaError_t chunk_prep(const ChunkArgs& a, void* scratch, cudaStream_t stream);
+cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t stream);
 
 }  // namespace gdn

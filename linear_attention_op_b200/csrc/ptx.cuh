@@ -211,6 +211,15 @@ __host__ __device__ constexpr uint32_t idesc_dense(int fmt, int M, int N) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization may start
+// before the previous kernel in the stream has finished; griddep_wait() blocks the calling thread until
+// that kernel has completed and its writes are visible (a no-op for ordinary launches), and
+// griddep_launch_dependents() lets the next such kernel start early.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------------------------
 // Clusters and distributed shared memory
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {

@@ -31,11 +31,15 @@ __global__ void __launch_bounds__(kRecThreads, 2) recurrence_kernel(RecurrenceAr
   __shared__ float s_red[4][4];
   __shared__ float s_scal[2];
 
+  griddep_launch_dependents();  // the successor (out_proj) only reads y after waiting for this kernel
   float* S = a.state + (static_cast<int64_t>(b) * a.Hv + h) * kHeadDim * kHeadDim;
   float4 st[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i)
     st[i] = __ldcs(reinterpret_cast<const float4*>(S + (r0 + i) * kHeadDim + c0));
+  // The state is not written by the kernel this one may overlap (the in_proj GEMM of the same call, which
+  // itself started only after the previous call had finished); the token inputs are.
+  griddep_wait();
 
 #pragma unroll 1
   for (int t = 0; t < a.T; ++t) {
@@ -134,11 +138,19 @@ __global__ void __launch_bounds__(kRecThreads, 2) recurrence_kernel(RecurrenceAr
   for (int i = 0; i < 16; ++i) __stcs(reinterpret_cast<float4*>(S + (r0 + i) * kHeadDim + c0), st[i]);
 }
 
-cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream) {
+cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream, bool pdl) {
   if (a.B <= 0 || a.T <= 0 || a.Hk <= 0 || a.Hv <= 0 || a.Hv % a.Hk) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.B * a.Hv));
+  cfg.blockDim = dim3(kRecThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
   count_launch();
-  recurrence_kernel<<<a.B * a.Hv, kRecThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return cudaLaunchKernelEx(&cfg, recurrence_kernel, a);
 }
 
 }  // namespace gdn

@@ -218,7 +218,7 @@ class Qwen35GatedDeltaNet:
         return other
 
     def set_stage_events(self, events: list | None) -> None:
-        """Have every forward record up to 6 timing events at its stage boundaries (see
+        """Have every forward record up to 7 timing events at its stage boundaries (see
         gdn_layer_set_stage_events); None disables."""
         if not events:
             call("gdn_layer_set_stage_events", self._h.handle, None, 0)
