@@ -55,17 +55,16 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bflo
   lo = __float2bfloat16_rn(x - __bfloat162float(hi));
 }
 
-// Pack 8 floats into hi and lo uint4 (8 bf16 each).
+// Pack 8 floats into hi and lo uint4 (8 bf16 each): hi = bf16(x), lo = bf16(x - hi), two lanes at a time.
 __device__ __forceinline__ void pack8(const float* x, uint4& hi, uint4& lo) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    __nv_bfloat16 h0, l0, h1, l1;
-    split_bf16(x[2 * i], h0, l0);
-    split_bf16(x[2 * i + 1], h1, l1);
-    __nv_bfloat162 hh(h0, h1), ll(l0, l1);
-    h[i] = *reinterpret_cast<uint32_t*>(&hh);
-    l[i] = *reinterpret_cast<uint32_t*>(&ll);
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    const float2 hf = __bfloat1622float2(hh);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[i] = *reinterpret_cast<const uint32_t*>(&ll);
   }
   hi = make_uint4(h[0], h[1], h[2], h[3]);
   lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -301,14 +300,14 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int s = s0 + i;
-        sm.m[t_row * kLdF + s] = s < t_row ? bt * acc[i] * expf(Gt - sm.G[s]) : 0.f;
+        sm.m[t_row * kLdF + s] = s < t_row ? bt * acc[i] * __expf(Gt - sm.G[s]) : 0.f;
       }
     } else {
       float av[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int s = s0 + i;
-        av[i] = s <= t_row ? acc[i] * expf(Gt - sm.G[s]) : 0.f;
+        av[i] = s <= t_row ? acc[i] * __expf(Gt - sm.G[s]) : 0.f;
       }
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
@@ -394,6 +393,7 @@ struct StateSmem {
   uint8_t vn_h[16384];   // Vn^T hi
   float gates[2][4 * kC];  // double-buffered beta | e^G | e^(G_C - G)
   float red[4][kC];
+  float rstd[kC];
   uint64_t bar_kq, bar_kt, bar_t, bar_g[2], bar_mma[3];
   uint32_t tmem;
   int abort;
@@ -543,9 +543,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
       float ks[32];
       tmem_ld32(tmem + lane_base + kColP1 + 32 * half, ks);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int t = 32 * half + j;
-        ks[j] = g_beta[t] * (vt[j] - g_eG[t] * ks[j]);
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 bt = reinterpret_cast<const float4*>(g_beta + 32 * half)[j4];
+        const float4 eg = reinterpret_cast<const float4*>(g_eG + 32 * half)[j4];
+        ks[4 * j4] = bt.x * (vt[4 * j4] - eg.x * ks[4 * j4]);
+        ks[4 * j4 + 1] = bt.y * (vt[4 * j4 + 1] - eg.y * ks[4 * j4 + 1]);
+        ks[4 * j4 + 2] = bt.z * (vt[4 * j4 + 2] - eg.z * ks[4 * j4 + 2]);
+        ks[4 * j4 + 3] = bt.w * (vt[4 * j4 + 3] - eg.w * ks[4 * j4 + 3]);
       }
       write_row32(sm.rv_h, sm.rv_l, v, 32 * half, ks);
     }
@@ -574,7 +578,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
       tmem_ld32(tmem + lane_base + kColVn + 32 * half, vn);
       write_row32(sm.vn_h, nullptr, v, 32 * half, vn);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) vn[j] *= g_eCG[32 * half + j];
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 e = reinterpret_cast<const float4*>(g_eCG + 32 * half)[j4];
+        vn[4 * j4] *= e.x;
+        vn[4 * j4 + 1] *= e.y;
+        vn[4 * j4 + 2] *= e.z;
+        vn[4 * j4 + 3] *= e.w;
+      }
       write_row32(sm.rv_h, sm.rv_l, v, 32 * half, vn);
     }
     fence_async_smem();
@@ -614,10 +624,15 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
       tmem_ld32(tmem + lane_base + kColAv + 32 * half, av);
       float a[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        o[j] = g_eG[32 * half + j] * o[j] + av[j];
-        a[j] = o[j] * o[j];
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 eg = reinterpret_cast<const float4*>(g_eG + 32 * half)[j4];
+        o[4 * j4] = eg.x * o[4 * j4] + av[4 * j4];
+        o[4 * j4 + 1] = eg.y * o[4 * j4 + 1] + av[4 * j4 + 1];
+        o[4 * j4 + 2] = eg.z * o[4 * j4 + 2] + av[4 * j4 + 2];
+        o[4 * j4 + 3] = eg.w * o[4 * j4 + 3] + av[4 * j4 + 3];
       }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a[j] = o[j] * o[j];
       // Butterfly: after the 5 steps lane l holds the warp's sum for t index 32 half + l.
       butterfly_step<16>(a, lane);
       butterfly_step<8>(a, lane);
@@ -641,15 +656,20 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
         write_row32(sm.st_h + half * 16384, sm.st_l + half * 16384, v, 32 * c32, S + 32 * c32);
     }
     __syncthreads();  // red[] complete
+    if (tid < kC)
+      sm.rstd[tid] = rsqrtf((sm.red[0][tid] + sm.red[1][tid] + sm.red[2][tid] + sm.red[3][tid]) * (1.0f / kD) + p.eps);
+    __syncthreads();
     {
       __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(p.y) + static_cast<int64_t>(h) * kD + v;
       const int64_t y_ld = static_cast<int64_t>(p.Hv) * kD;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int t = 32 * half + j;
-        if (t < L) {
-          const float ms = (sm.red[0][t] + sm.red[1][t] + sm.red[2][t] + sm.red[3][t]) * (1.0f / kD);
-          yb[(row0 + t) * y_ld] = __float2bfloat16_rn(o[j] * rsqrtf(ms + p.eps) * w_norm * silu_f(zt[j]));
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 rs = reinterpret_cast<const float4*>(sm.rstd + 32 * half)[j4];
+        const float r4[4] = {rs.x, rs.y, rs.z, rs.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 4 * j4 + u, t = 32 * half + j;
+          if (t < L) yb[(row0 + t) * y_ld] = __float2bfloat16_rn(o[j] * r4[u] * w_norm * silu_fast(zt[j]));
         }
       }
     }

@@ -5,6 +5,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -92,8 +93,8 @@ struct gdn_layer {
   int kd = 0, vd = 0, conv_dim = 0; // local channel counts
   int rows = 0;                     // fused in_proj rows: conv_dim + vd + 2 hv
   int proj_ld = 0;                  // row stride of the in_proj output buffer: rows rounded up to 8
-  __nv_bfloat16* w_in = nullptr;    // [rows, hidden]: [q | k | v | z | a | b]
-  __nv_bfloat16* w_out = nullptr;   // [hidden, vd]
+  __nv_bfloat16* w_in = nullptr;    // [rows, hidden] = [q | k | v | z | a | b], pre-tiled (tiled_weight_bytes)
+  __nv_bfloat16* w_out = nullptr;   // [hidden, vd], pre-tiled
   float* conv_w = nullptr;          // [conv_dim, 4]
   float* a_log = nullptr;           // [hv]
   float* dt_bias = nullptr;         // [hv]
@@ -189,14 +190,18 @@ extern "C" gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* 
   const int64_t v0 = static_cast<int64_t>(tp_rank) * L->vd;  // first local v/z channel
   const int64_t hv0 = static_cast<int64_t>(tp_rank) * L->hv; // first local v-head
 
+  __nv_bfloat16* w_in_rm = nullptr;   // row-major staging copies, tiled into L->w_in / L->w_out below
+  __nv_bfloat16* w_out_rm = nullptr;
   auto run = [&]() -> gdn_status {
-    GDN_CUDA(cudaMalloc(&L->w_in, static_cast<size_t>(L->rows) * h * 2));
-    GDN_CUDA(cudaMalloc(&L->w_out, static_cast<size_t>(h) * L->vd * 2));
+    GDN_CUDA(cudaMalloc(&w_in_rm, static_cast<size_t>(L->rows) * h * 2));
+    GDN_CUDA(cudaMalloc(&w_out_rm, static_cast<size_t>(h) * L->vd * 2));
+    GDN_CUDA(cudaMalloc(&L->w_in, tiled_weight_bytes(L->rows, static_cast<int>(h))));
+    GDN_CUDA(cudaMalloc(&L->w_out, tiled_weight_bytes(static_cast<int>(h), L->vd)));
     GDN_CUDA(cudaMalloc(&L->conv_w, static_cast<size_t>(L->conv_dim) * 4 * 4));
     GDN_CUDA(cudaMalloc(&L->a_log, L->hv * 4));
     GDN_CUDA(cudaMalloc(&L->dt_bias, L->hv * 4));
     GDN_CUDA(cudaMalloc(&L->norm_w, kHeadDim * 4));
-    char* win = reinterpret_cast<char*>(L->w_in);
+    char* win = reinterpret_cast<char*>(w_in_rm);
     int64_t r = 0;
     // q, k, v rows of in_proj_qkv, then z, a, b
     GDN_CUDA(copy_rows(win + r * h * 2, w->w_qkv, h, k0, L->kd, h, 2)); r += L->kd;
@@ -215,12 +220,16 @@ extern "C" gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* 
     GDN_CUDA(cudaMemcpy(L->norm_w, w->norm_w, kHeadDim * 4, cudaMemcpyDefault));
     // out_proj columns of the local v-heads: [hidden, vd] slice of [hidden, Hv*128]
     const int64_t vd_g = static_cast<int64_t>(d.num_v_heads) * kHeadDim;
-    GDN_CUDA(cudaMemcpy2D(L->w_out, L->vd * 2, reinterpret_cast<const char*>(w->w_out) + v0 * 2, vd_g * 2,
+    GDN_CUDA(cudaMemcpy2D(w_out_rm, L->vd * 2, reinterpret_cast<const char*>(w->w_out) + v0 * 2, vd_g * 2,
                           L->vd * 2, h, cudaMemcpyDefault));
+    GDN_CUDA(tile_weights_bf16(w_in_rm, h, L->rows, static_cast<int>(h), L->w_in, nullptr));
+    GDN_CUDA(tile_weights_bf16(w_out_rm, L->vd, static_cast<int>(h), L->vd, L->w_out, nullptr));
     GDN_CUDA(cudaDeviceSynchronize());
     return GDN_OK;
   };
   const gdn_status st = run();
+  if (w_in_rm) cudaFree(w_in_rm);
+  if (w_out_rm) cudaFree(w_out_rm);
   if (st != GDN_OK) {
     free_layer(L);
     return st;
@@ -299,6 +308,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   if (T == 1) {
     // ---- decode: in_proj (weights as the 128-row operand) with conv + gating fused into the epilogue
     GemmEpiArgs ep;
+    ep.a_tiled = L->w_in;
     ep.out = proj;
     ep.ld = L->proj_ld;
     ep.conv_rows = L->conv_dim;
@@ -331,6 +341,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     GemmEpiArgs eo;
     eo.out = out;
     eo.ld = h;
+    eo.a_tiled = L->w_out;
     GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
     GDN_CUDA(stage_mark(L, 5, stream));
   } else {
@@ -338,6 +349,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     GemmEpiArgs ep;
     ep.out = proj;
     ep.ld = L->proj_ld;
+    ep.b_tiled = L->w_in;
     GDN_CUDA(gemm_bf16_tn(x, h, L->w_in, h, static_cast<int>(n), L->rows, h, kEpiStoreF32, ep, 1, stream, true));
     GDN_CUDA(stage_mark(L, 1, stream));
     GDN_CUDA(conv_prefill(proj, L->proj_ld, qkv, L->conv_dim, L->conv_w, conv_state, B, T, L->conv_dim, stream));
@@ -356,6 +368,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     GemmEpiArgs eo;
     eo.out = out;
     eo.ld = h;
+    eo.b_tiled = L->w_out;
     GDN_CUDA(gemm_bf16_tn(y, L->vd, L->w_out, L->vd, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, 1, stream, true));
     GDN_CUDA(stage_mark(L, 5, stream));
   }
@@ -436,6 +449,7 @@ extern "C" gdn_status gdn_layer_decode_static(gdn_layer* L, const uint16_t* x, i
   ep.conv_state = conv_state;
   ep.a_log = L->a_log;
   ep.dt_bias = L->dt_bias;
+  ep.a_tiled = L->w_in;
   GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream));
   RecurrenceArgs ra;
   ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
@@ -455,6 +469,7 @@ extern "C" gdn_status gdn_layer_decode_static(gdn_layer* L, const uint16_t* x, i
   GemmEpiArgs eo;
   eo.out = out;
   eo.ld = h;
+  eo.a_tiled = L->w_out;
   GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream));
   return GDN_OK;
 }

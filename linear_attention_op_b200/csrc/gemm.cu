@@ -17,6 +17,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -46,9 +47,27 @@ struct GemmCfg {
   static_assert(BN * kBM * 4 <= STAGES * kStageBytes, "split-K partial tile must fit in the stage ring");
 };
 
+// Conv history of row m (a conv channel) for tokens n0 .. n0 + 15: conv_state rows 0..2, oldest first.
+struct ConvHist {
+  float h[3][16];
+};
+
+__device__ __forceinline__ void conv_prefetch(const GemmEpiArgs& ep, int m, int n0, int N, ConvHist& hs) {
+  const int cr = ep.conv_rows;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int n = n0 + j;
+    const float* cs = ep.conv_state + static_cast<int64_t>(n < N ? n : 0) * 3 * cr + m;
+    hs.h[0][j] = cs[0];
+    hs.h[1][j] = cs[cr];
+    hs.h[2][j] = cs[2 * cr];
+  }
+}
+
+// For kEpiDecodeInProj conv rows `hs` must hold the conv history of (m, n0 .. n0 + 15) (conv_prefetch).
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0, int M, int N,
-                                           const float (&v)[16]) {
+                                           const float (&v)[16], const ConvHist& hs) {
   if (m >= M) return;
   if constexpr (EPI == kEpiStoreF32) {
     float* row = static_cast<float*>(ep.out) + static_cast<int64_t>(m) * ep.ld + n0;
@@ -96,24 +115,16 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
       // state rolls by one (9B/kernels/layer_reader.cpp:184-197; HF torch_causal_conv1d_update).  All 48
       // history loads are issued before any store so their latencies overlap.
       const float4 w = *reinterpret_cast<const float4*>(ep.conv_w + static_cast<int64_t>(m) * 4);
-      float h0[16], h1[16], h2[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = n0 + j;
-        const float* cs = ep.conv_state + static_cast<int64_t>(n < N ? n : 0) * 3 * cr + m;
-        h0[j] = cs[0];
-        h1[j] = cs[cr];
-        h2[j] = cs[2 * cr];
-      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int n = n0 + j;
         if (n < N) {
           float* cs = ep.conv_state + static_cast<int64_t>(n) * 3 * cr + m;
-          cs[0] = h1[j];
-          cs[cr] = h2[j];
+          cs[0] = hs.h[1][j];
+          cs[cr] = hs.h[2][j];
           cs[2 * cr] = v[j];
-          out[static_cast<int64_t>(n) * ep.ld + m] = silu_f(w.x * h0[j] + w.y * h1[j] + w.z * h2[j] + w.w * v[j]);
+          out[static_cast<int64_t>(n) * ep.ld + m] =
+              silu_f(w.x * hs.h[0][j] + w.y * hs.h[1][j] + w.z * hs.h[2][j] + w.w * v[j]);
         }
       }
     } else if (m < cr + ep.z_rows) {
@@ -139,7 +150,8 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, int ksplit, int n_tiles, int group_m, int trigger_early, GemmEpiArgs ep) {
+                   int K, int ksplit, int n_tiles, int group_m, int trigger_early, const uint8_t* a_tiled,
+                   const uint8_t* b_tiled, GemmEpiArgs ep) {
   using C = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -172,8 +184,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(accum, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    if (!a_tiled) tma_prefetch_desc(&tmA);
+    if (!b_tiled) tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -193,26 +205,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint64_t pol_b = policy_evict_last();
       // The weight operand (A for the transposed decode epilogues, B otherwise) does not depend on the
       // previous kernel: its first stages are requested before waiting for that kernel to finish.
+      // Operands stored pre-tiled (the layer's weights) arrive as contiguous 16 KB blocks, each already
+      // in the 128B-swizzled shared-memory layout of a 128-row x 64 tile, by 1D bulk copies; the others
+      // through their tensor maps.
+      const int kbt = (K + kBK - 1) / kBK;
+      auto load_a = [&](int s, int kb) {
+        if (a_tiled)
+          bulk_load_hint(sA + s * C::kABytes, a_tiled + (static_cast<int64_t>(m_tile) * kbt + kb) * 16384, 16384,
+                         &full[s], pol_a);
+        else
+          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, m_tile * kBM, pol_a);
+      };
+      auto load_b = [&](int s, int kb) {
+        if (b_tiled) {
+#pragma unroll
+          for (int q = 0; q < BN / 128; ++q)
+            bulk_load_hint(sB + s * C::kBBytes + q * 16384,
+                           b_tiled + (static_cast<int64_t>(n_tile * (BN / 128) + q) * kbt + kb) * 16384, 16384,
+                           &full[s], pol_b);
+        } else {
+          tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, n_tile * BN, pol_b);
+        }
+      };
       const int pre = nk < STAGES ? nk : STAGES;
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-        const int kx = (kb0 + i) * kBK;
-        if (a_streamed) tma_load_2d(sA + i * C::kABytes, &tmA, &full[i], kx, m_tile * kBM, pol_a);
-        else tma_load_2d(sB + i * C::kBBytes, &tmB, &full[i], kx, n_tile * BN, pol_b);
+        if (a_streamed) load_a(i, kb0 + i);
+        else load_b(i, kb0 + i);
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i) {
-        const int kx = (kb0 + i) * kBK;
-        if (a_streamed) tma_load_2d(sB + i * C::kBBytes, &tmB, &full[i], kx, n_tile * BN, pol_b);
-        else tma_load_2d(sA + i * C::kABytes, &tmA, &full[i], kx, m_tile * kBM, pol_a);
+        if (a_streamed) load_b(i, kb0 + i);
+        else load_a(i, kb0 + i);
       }
       for (int i = pre; i < nk; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, kErrWaitSmemEmpty)) break;
         mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        const int kx = (kb0 + i) * kBK;
-        tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kx, m_tile * kBM, pol_a);
-        tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kx, n_tile * BN, pol_b);
+        load_a(s, kb0 + i);
+        load_b(s, kb0 + i);
       }
     }
     __syncwarp();
@@ -239,8 +270,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int r = q * 32 + lane;     // row inside the tile
   const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
   const bool epi_warp = warp >= 2;
+  // The decode in_proj epilogue reads the conv history of its first column chunk while the main loop runs.
+  ConvHist hist;
+  const int first_c0 = ksplit > 1 ? split * 16 : 0;
   if (epi_warp) {
     griddep_wait();  // the epilogue writes buffers the previous kernel may still read
+    if constexpr (EPI == kEpiDecodeInProj) {
+      const int m = m_tile * kBM + r;
+      if (m < M && m < ep.conv_rows && first_c0 < BN) conv_prefetch(ep, m, n_tile * BN + first_c0, N, hist);
+    }
     mbar_wait(accum, 0, kErrWaitAccum);
     tc_fence_after();
   }
@@ -251,7 +289,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(t_row + c0, v);
-        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
+        if constexpr (EPI == kEpiDecodeInProj)
+          if (c0 != first_c0 && m < M && m < ep.conv_rows) conv_prefetch(ep, m, n_tile * BN + c0, N, hist);
+        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v, hist);
       }
     }
   } else {
@@ -295,7 +335,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
+        if constexpr (EPI == kEpiDecodeInProj)
+          if (c0 != first_c0 && m < M && m < ep.conv_rows) conv_prefetch(ep, m, n_tile * BN + c0, N, hist);
+        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v, hist);
       }
     }
     __syncwarp();
@@ -422,7 +464,8 @@ static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int
   cfg.attrs = attr;
   cfg.numAttrs = na;
   count_launch();
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, n_tiles, group_m, trigger ? 1 : 0, ep);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, n_tiles, group_m, trigger ? 1 : 0,
+                            static_cast<const uint8_t*>(ep.a_tiled), static_cast<const uint8_t*>(ep.b_tiled), ep);
 }
 
 template <int BN, int STAGES>
@@ -447,11 +490,14 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   else if (N <= 64) BN = 64;
   else if (N <= 128) BN = 128;
   else BN = 256;
+  if (ep.b_tiled && BN < 128) BN = 128;  // a tiled B operand comes in whole 128-row blocks
+  if ((ep.a_tiled && A != ep.a_tiled) || (ep.b_tiled && B != ep.b_tiled)) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
-  cudaError_t e = make_tmap(&ta, A, M, K, lda, kBM);
-  if (e != cudaSuccess) return e;
-  e = make_tmap(&tb, B, N, K, ldb, BN);
-  if (e != cudaSuccess) return e;
+  std::memset(&ta, 0, sizeof(ta));
+  std::memset(&tb, 0, sizeof(tb));
+  cudaError_t e = cudaSuccess;
+  if (!ep.a_tiled && (e = make_tmap(&ta, A, M, K, lda, kBM)) != cudaSuccess) return e;
+  if (!ep.b_tiled && (e = make_tmap(&tb, B, N, K, ldb, BN)) != cudaSuccess) return e;
   // Skinny (decode) tiles use a 3-stage ring (< 75 KB) so three CTAs share an SM and a split-K launch fits
   // in one wave of clusters; wide tiles take the whole SM.
   switch (BN) {
@@ -461,6 +507,39 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
     case 128: return dispatch_epi<128, 6>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
     default: return dispatch_epi<256, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Pre-tiled weights
+// ---------------------------------------------------------------------------------------------
+size_t tiled_weight_bytes(int rows, int cols) {
+  const int64_t mt = ((rows + kBM - 1) / kBM + 1) & ~1;  // even number of 128-row blocks (pairs for BN = 256)
+  return static_cast<size_t>(mt) * ((cols + kBK - 1) / kBK) * 16384;
+}
+
+// dst block (mt, kb) = rows [128 mt, +128) x cols [64 kb, +64) of src, in the K-major 128B-swizzled layout
+// (row r at r * 128 bytes, 16-byte chunk c at chunk c ^ (r % 8)); rows past `rows` are zero.
+__global__ void tile_weights_kernel(const uint16_t* __restrict__ src, int64_t ld, int rows, int cols,
+                                    uint4* __restrict__ dst, int64_t nchunks) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= nchunks) return;
+  const int kbt = (cols + kBK - 1) / kBK;
+  const int64_t blk = i >> 10;  // 1024 chunks of 16 B per 16 KB block
+  const int w = static_cast<int>(i & 1023), r = w >> 3, cs = w & 7;
+  const int mt = static_cast<int>(blk / kbt), kb = static_cast<int>(blk % kbt);
+  const int row = mt * kBM + r, col = kb * kBK + ((cs ^ (r & 7)) << 3);
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (row < rows && col < cols) v = *reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row) * ld + col);
+  dst[i] = v;
+}
+
+cudaError_t tile_weights_bf16(const void* src, int64_t ld, int rows, int cols, void* dst, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0 || (cols & 7) || (ld & 7) || (reinterpret_cast<uintptr_t>(src) & 15)) return cudaErrorInvalidValue;
+  const int64_t n = static_cast<int64_t>(tiled_weight_bytes(rows, cols) / 16);
+  count_launch();
+  tile_weights_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      static_cast<const uint16_t*>(src), ld, rows, cols, static_cast<uint4*>(dst), n);
+  return cudaGetLastError();
 }
 
 }  // namespace gdn

@@ -30,11 +30,14 @@ struct GemmEpiArgs {
   float* conv_state = nullptr;    // [N, 3, conv_rows] (N = number of sequences = GEMM N)
   const float* a_log = nullptr;   // [nheads]
   const float* dt_bias = nullptr; // [nheads]
+  // Operands stored pre-tiled by tile_weights_bf16 (then A / B must equal these pointers; lda / ldb unused).
+  const void* a_tiled = nullptr;
+  const void* b_tiled = nullptr;
 };
 
-// A: [M, K] bf16 row-major with row stride lda (elements); B: [N, K] bf16 row-major with row stride ldb.
-// ksplit > 1 splits K over a cluster of ksplit CTAs whose partial tiles are summed through
-// distributed shared memory (no global workspace).  ksplit = 0 picks a value.
+// A: [M, K] bf16 row-major with row stride lda (elements); B: [N, K] bf16 row-major with row stride ldb
+// (or pre-tiled, see GemmEpiArgs).  ksplit > 1 splits K over a cluster of ksplit CTAs whose partial tiles
+// are summed through distributed shared memory (no global workspace).  ksplit = 0 picks a value.
 // pdl: launch with programmatic stream serialization (the kernel may start while the previous kernel in
 // the stream is still running; it prefetches the weight operand -- A for the transposed epilogues, B
 // otherwise -- and waits for the previous kernel before touching anything else).
@@ -44,6 +47,12 @@ struct GemmEpiArgs {
 cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
                          const GemmEpiArgs& args, int ksplit, cudaStream_t stream, bool pdl = false,
                          bool trigger = false);
+
+// Weights kept in the GEMM's streaming layout: [ceil(rows/128), rounded up to even][cols/64] blocks of
+// 16 KB, each block the 128B-swizzled shared-memory image of a 128 x 64 bf16 tile, so that a K-slice of
+// an M-tile is one contiguous run of HBM.
+size_t tiled_weight_bytes(int rows, int cols);
+cudaError_t tile_weights_bf16(const void* src, int64_t ld, int rows, int cols, void* dst, cudaStream_t stream);
 
 // Number of kernel launches issued by this library since load (for the benchmark's launch count).
 uint64_t launch_count();

@@ -114,6 +114,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 1D bulk copy global -> shared (contiguous bytes, 16-byte aligned) with an L2 cache policy.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(cache_hint)
+      : "memory");
+}
+
 // L2 cache policies (createpolicy): weights are streamed once, activations are re-read by many CTAs.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
@@ -249,6 +259,8 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
 // Math helpers (CUDA's own expf/log1pf; no re-implementation of library math)
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// Fast SiLU (CUDA's __expf / __fdividef intrinsics) for the output gate, whose result is rounded to bf16.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 // torch.nn.functional.softplus with beta = 1, threshold = 20.
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }

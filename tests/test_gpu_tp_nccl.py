@@ -1,0 +1,82 @@
+"""Head-parallel layer over 2 (or 4) GPUs with the library's NCCL communicator: every rank gets the full,
+all-reduced output, and the ranks' states tile the single-GPU state.  Skipped with fewer GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+
+from tests._util import requires_b200
+
+pytestmark = [pytest.mark.gpu, requires_b200]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        import datetime
+
+        import torch.distributed as dist
+
+        from linear_attention_op_b200 import Qwen35GatedDeltaNet, device_error
+        from linear_attention_op_b200.tp import Communicator
+        from oracle import gdn_oracle as O
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+        comm = Communicator.from_process_group()
+        w = O.make_weights(1024, 16, 32, seed=7)
+        x = O.make_hidden(2, 70, 1024, seed=7)
+        want, s_want, c_want = O.layer_forward(w, x, mode="chunk")
+        xd = O.make_hidden(2, 1, 1024, seed=8)
+        want_d, s_want_d, _ = O.layer_forward(w, xd, s_want, c_want, mode="recurrent")
+        layer = Qwen35GatedDeltaNet(weights=w, batch=2, tp_rank=rank, tp_size=world, comm=comm)
+        y = layer(x)
+        s_loc = layer.get_recurrent_state()
+        yd = layer(xd)
+        s_loc_d = layer.get_recurrent_state()
+        err = device_error()
+        hv = 32 // world
+        res = dict(
+            out=O.max_abs_rel(y.float(), want), state=O.max_abs_rel(s_loc, s_want[:, rank * hv:(rank + 1) * hv]),
+            out_dec=O.max_abs_rel(yd.float(), want_d),
+            state_dec=O.max_abs_rel(s_loc_d, s_want_d[:, rank * hv:(rank + 1) * hv]), err=err)
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as e:  # report instead of hanging the parent
+        import traceback
+
+        q.put((rank, {"exc": traceback.format_exc()}))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_layer_nccl(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    for rank in range(world):
+        r = results[rank]
+        assert "exc" not in r, r.get("exc")
+        print(rank, r)
+        assert r["err"] == 0
+        assert r["out"] <= 2e-2 and r["out_dec"] <= 2e-2, r
+        assert r["state"] <= 1e-3 and r["state_dec"] <= 1e-3, r

@@ -48,7 +48,7 @@ def test_static_decode_matches_forward_two_calls(hidden, hk, hv, B):
     for t in range(2):
         check(f"static decode call {t}", got[t], want[t])
     check("static decode state", layer.rec_state, want_s, max_rel=STATE_TOL)
-    check("static decode conv state", layer.conv_state, want_c, max_rel=1e-6)
+    check("static decode conv state", layer.conv_state, want_c, max_rel=1e-4)
 
 
 def test_static_decode_rejects_batch_beyond_scratch():
