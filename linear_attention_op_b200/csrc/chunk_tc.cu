@@ -231,22 +231,22 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
   __syncwarp();
   const bool ok = mbar_wait(&sm.bar, 0, kErrWaitAccum);
   tc_fence_after();
-  // Row r of the accumulator: r < 64 -> (k_r . k_s), r >= 64 -> (q_(r-64) . k_s); this thread: 32 columns.
-  const int q4 = warp & 3, half = warp >> 2;
+  // Row r of the accumulator: r < 64 -> (k_r . k_s), r >= 64 -> (q_(r-64) . k_s).  Warp w reads the rows of
+  // its TMEM lane quarter (w % 4), all 64 columns: the two warp groups (warps 0-3, 4-7) each hold the whole
+  // accumulator and work on different v-heads of the GQA group concurrently.
+  const int q4 = warp & 3, grp = warp >> 2, gtid = tid & 127;
   const int r = q4 * 32 + lane;
-  float acc[32];
-  {
+  float acc[64];
+#pragma unroll
+  for (int c16 = 0; c16 < 4; ++c16) {
     float v[16];
-    tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * half, v);
+    tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 16 * c16, v);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = v[i];
-    tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * half + 16, v);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[16 + i] = v[i];
+    for (int i = 0; i < 16; ++i) acc[16 * c16 + i] = v[i];
   }
-  const int s0 = 32 * half;
   const int t_row = r & 63;
   const bool is_k = r < 64;
+  const int tr = gtid >> 1, th = gtid & 1;  // T image writer: (row, 32-column half)
 
   // ---- the gate-independent operand image of this (sequence, k-head, chunk)
   {
@@ -281,99 +281,110 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
     }
   }
 
-  for (int j = 0; j < ratio && ok; ++j) {
+  __syncthreads();  // the [K; Q] tiles are free: group 1 works in that space from here on
+  float* gm = grp ? reinterpret_cast<float*>(sm.kq_h) : sm.m;          // M, then read-only
+  float* gt = grp ? gm + kC * kLdF : sm.t;                             // T
+  float* gx = grp ? gt + kC * kLdF : sm.x;                             // block-inverse temporaries
+  float* gG = grp ? gx + 3 * 256 : sm.G;
+  float* gB = gG + kC;                                                 // beta
+  float* gE = gB + kC;                                                 // e^G
+  float* gC = gE + kC;                                                 // e^(G_C - G)
+  if (!grp) {
+    gB = sm.beta;
+    gE = sm.eG;
+    gC = sm.eCG;
+  }
+  auto group_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory"); };
+
+  for (int j = grp; j < ratio && ok; j += 2) {
     const int h = kh * ratio + j;
-    if (warp == 0)
-      chunk_gates(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, h, -expf(p.a_log[h]), p.dt_bias[h], lane, sm.G,
-                  sm.beta, sm.eG, sm.eCG);
-    __syncthreads();
+    if (q4 == 0)
+      chunk_gates(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, h, -expf(p.a_log[h]), p.dt_bias[h], lane, gG, gB,
+                  gE, gC);
+    // strictly upper blocks of T are zero
+    for (int idx = gtid; idx < 6 * 256; idx += 128) {
+      const int blk = idx >> 8, e = idx & 255;
+      const int ra = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+      const int cb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+      gt[(ra * 16 + (e >> 4)) * kLdF + cb * 16 + (e & 15)] = 0.f;
+    }
+    group_sync();
     uint8_t* img = timg + ((static_cast<int64_t>(b) * p.Hv + h) * nchunks + ch) * kTImageBytes;
-    if (tid < kC) {
+    if (gtid < kC) {
       float* gi = reinterpret_cast<float*>(img + kTGateOff);
-      gi[tid] = sm.beta[tid];
-      gi[kC + tid] = sm.eG[tid];
-      gi[2 * kC + tid] = sm.eCG[tid];
+      gi[gtid] = gB[gtid];
+      gi[kC + gtid] = gE[gtid];
+      gi[2 * kC + gtid] = gC[gtid];
     }
-    const float Gt = sm.G[t_row];
+    const float Gt = gG[t_row];
     if (is_k) {
-      const float bt = sm.beta[t_row];
+      const float bt = gB[t_row];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int s = s0 + i;
-        sm.m[t_row * kLdF + s] = s < t_row ? bt * acc[i] * __expf(Gt - sm.G[s]) : 0.f;
-      }
+      for (int s = 0; s < kC; ++s) gm[t_row * kLdF + s] = s < t_row ? bt * acc[s] * __expf(Gt - gG[s]) : 0.f;
     } else {
-      float av[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int s = s0 + i;
-        av[i] = s <= t_row ? acc[i] * __expf(Gt - sm.G[s]) : 0.f;
-      }
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float av[8];
 #pragma unroll
-      for (int c8 = 0; c8 < 4; ++c8) {
+        for (int i = 0; i < 8; ++i) {
+          const int s = 8 * c8 + i;
+          av[i] = s <= t_row ? acc[s] * __expf(Gt - gG[s]) : 0.f;
+        }
         uint4 hi, lo;
-        pack8(av + 8 * c8, hi, lo);
-        *reinterpret_cast<uint4*>(img + 16384 + sw_off(t_row, s0 + 8 * c8)) = hi;  // A tile (hi only)
+        pack8(av, hi, lo);
+        *reinterpret_cast<uint4*>(img + 16384 + sw_off(t_row, 8 * c8)) = hi;  // A tile (hi only)
       }
     }
-    __syncthreads();
+    group_sync();
     // ---- T = (I + M)^-1: 16 x 16 diagonal blocks by forward substitution, then off-diagonal blocks.
-    if (warp < 4) {
-      const int o = warp * 16, jj = lane & 15;
+    {
+      const int o = q4 * 16, jj = lane & 15;
       if (lane < 16)
-        for (int i = 0; i < 16; ++i) sm.t[(o + i) * kLdF + o + jj] = (i == jj) ? 1.f : 0.f;
+        for (int i = 0; i < 16; ++i) gt[(o + i) * kLdF + o + jj] = (i == jj) ? 1.f : 0.f;
       __syncwarp();
       for (int i = 1; i < 16; ++i) {
         float a = 0.f;
         if (lane < 16 && jj < i)
-          for (int mm = jj; mm < i; ++mm) a += sm.m[(o + i) * kLdF + o + mm] * sm.t[(o + mm) * kLdF + o + jj];
+          for (int mm = jj; mm < i; ++mm) a += gm[(o + i) * kLdF + o + mm] * gt[(o + mm) * kLdF + o + jj];
         __syncwarp();
-        if (lane < 16 && jj < i) sm.t[(o + i) * kLdF + o + jj] = -a;
+        if (lane < 16 && jj < i) gt[(o + i) * kLdF + o + jj] = -a;
         __syncwarp();
-      }
-    } else {
-      for (int idx = tid - 128; idx < 6 * 256; idx += 128) {  // strictly upper blocks of T are zero
-        const int blk = idx >> 8, e = idx & 255;
-        const int ra = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-        const int cb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-        sm.t[(ra * 16 + (e >> 4)) * kLdF + cb * 16 + (e & 15)] = 0.f;
       }
     }
-    __syncthreads();
+    group_sync();
     for (int d = 1; d < 4; ++d) {
       const int nb = 4 - d;
-      for (int idx = tid; idx < nb * 256; idx += kThreads) {  // X = sum_{c=b}^{a-1} M_ac T_cb
+      for (int idx = gtid; idx < nb * 256; idx += 128) {  // X = sum_{c=b}^{a-1} M_ac T_cb
         const int bb = idx >> 8, e = idx & 255, i = e >> 4, jj = e & 15, aa = bb + d;
         float a = 0.f;
         for (int c = bb; c < aa; ++c)
 #pragma unroll 4
-          for (int mm = 0; mm < 16; ++mm) a += sm.m[(aa * 16 + i) * kLdF + c * 16 + mm] * sm.t[(c * 16 + mm) * kLdF + bb * 16 + jj];
-        sm.x[idx] = a;
+          for (int mm = 0; mm < 16; ++mm) a += gm[(aa * 16 + i) * kLdF + c * 16 + mm] * gt[(c * 16 + mm) * kLdF + bb * 16 + jj];
+        gx[idx] = a;
       }
-      __syncthreads();
-      for (int idx = tid; idx < nb * 256; idx += kThreads) {  // T_ab = -T_aa X
+      group_sync();
+      for (int idx = gtid; idx < nb * 256; idx += 128) {  // T_ab = -T_aa X
         const int bb = idx >> 8, e = idx & 255, i = e >> 4, jj = e & 15, aa = bb + d;
         float a = 0.f;
-        for (int mm = 0; mm <= i; ++mm) a += sm.t[(aa * 16 + i) * kLdF + aa * 16 + mm] * sm.x[bb * 256 + mm * 16 + jj];
-        sm.t[(aa * 16 + i) * kLdF + bb * 16 + jj] = -a;
+        for (int mm = 0; mm <= i; ++mm) a += gt[(aa * 16 + i) * kLdF + aa * 16 + mm] * gx[bb * 256 + mm * 16 + jj];
+        gt[(aa * 16 + i) * kLdF + bb * 16 + jj] = -a;
       }
-      __syncthreads();
+      group_sync();
     }
-    // ---- T image: hi at +0, lo at +8192; thread (row, 16-column quarter)
+    // ---- T image: hi at +0, lo at +8192; thread (row, 32-column half)
     {
-      const int tr = tid >> 2, cq = (tid & 3) * 16;
-      float tv[16];
+      float tv[32];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) tv[i] = sm.t[tr * kLdF + cq + i];
+      for (int i = 0; i < 32; ++i) tv[i] = gt[tr * kLdF + 32 * th + i];
 #pragma unroll
-      for (int c8 = 0; c8 < 2; ++c8) {
+      for (int c8 = 0; c8 < 4; ++c8) {
         uint4 hi, lo;
         pack8(tv + 8 * c8, hi, lo);
-        *reinterpret_cast<uint4*>(img + sw_off(tr, cq + 8 * c8)) = hi;
-        *reinterpret_cast<uint4*>(img + 8192 + sw_off(tr, cq + 8 * c8)) = lo;
+        *reinterpret_cast<uint4*>(img + sw_off(tr, 32 * th + 8 * c8)) = hi;
+        *reinterpret_cast<uint4*>(img + 8192 + sw_off(tr, 32 * th + 8 * c8)) = lo;
       }
     }
-    __syncthreads();
+    group_sync();
   }
   tc_fence_before();
   __syncthreads();
