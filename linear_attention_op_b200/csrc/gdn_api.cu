@@ -107,13 +107,21 @@ struct gdn_layer {
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// Workspace layout for n token rows in `chunks` (sequence, chunk) pairs:
-//   proj fp32 [n, proj_ld] | qkv fp32 [n, conv_dim] | y bf16 [n, vd] | chunk tile images
-static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks) {
-  return align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4) + align256(n * L->vd * 2) +
-         align256(chunk_prefill_scratch_bytes(1, 64, L->hk, L->hv) * static_cast<size_t>(chunks));
+// Workspace layout for n token rows in `chunks` (sequence, chunk) pairs (chunks >= B for prefill):
+//   proj fp32 [n, proj_ld] (conv channels already convolved) | y bf16 [n, vd] |
+//   conv tail fp32 [chunks, 3, conv_dim] | chunk tile images
+struct WsLayout {
+  size_t y, tail, chunk, total;
+};
+static WsLayout ws_layout(const gdn_layer* L, int64_t n, int64_t chunks) {
+  WsLayout o;
+  o.y = align256(n * L->proj_ld * 4);
+  o.tail = o.y + align256(n * L->vd * 2);
+  o.chunk = o.tail + align256(static_cast<size_t>(chunks) * 3 * L->conv_dim * 4);
+  o.total = o.chunk + align256(chunk_prefill_scratch_bytes(1, 64, L->hk, L->hv) * static_cast<size_t>(chunks));
+  return o;
 }
-
+static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks) { return ws_layout(L, n, chunks).total; }
 static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream) {
   const size_t need = workspace_bytes(L, n, chunks);
   if (need <= L->ws_bytes) return GDN_OK;
@@ -298,10 +306,11 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   if (st != GDN_OK) return st;
   const int h = L->dims.hidden;
   char* ws = static_cast<char*>(L->ws);
+  const WsLayout lay = ws_layout(L, n, chunks);
   float* proj = reinterpret_cast<float*>(ws);
-  float* qkv = reinterpret_cast<float*>(ws + align256(n * L->proj_ld * 4));
-  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4));
-  void* chunk_scratch = ws + align256(n * L->proj_ld * 4) + align256(n * L->conv_dim * 4) + align256(n * L->vd * 2);
+  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + lay.y);
+  float* conv_tail = reinterpret_cast<float*>(ws + lay.tail);
+  void* chunk_scratch = ws + lay.chunk;
   const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
 
   GDN_CUDA(stage_mark(L, 0, stream));
@@ -345,17 +354,22 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
     GDN_CUDA(stage_mark(L, 5, stream));
   } else {
-    // ---- prefill: in_proj -> conv -> chunked recurrence + gated RMSNorm -> out_proj
+    // ---- prefill: in_proj with the causal conv + SiLU fused into its epilogue -> conv-state roll ->
+    //      chunked recurrence + gated RMSNorm -> out_proj
     GemmEpiArgs ep;
     ep.out = proj;
     ep.ld = L->proj_ld;
-    ep.b_tiled = L->w_in;
-    GDN_CUDA(gemm_bf16_tn(x, h, L->w_in, h, static_cast<int>(n), L->rows, h, kEpiStoreF32, ep, 1, stream, true));
+    ep.conv_rows = L->conv_dim;
+    ep.conv_w = L->conv_w;
+    ep.conv_state = conv_state;
+    ep.seq_len = T;
+    ep.conv_tail = conv_tail;
+    GDN_CUDA(gemm_bf16_persistent(x, h, L->w_in, static_cast<int>(n), L->rows, h, kEpiPrefillInProj, ep, stream, true));
     GDN_CUDA(stage_mark(L, 1, stream));
-    GDN_CUDA(conv_prefill(proj, L->proj_ld, qkv, L->conv_dim, L->conv_w, conv_state, B, T, L->conv_dim, stream));
+    GDN_CUDA(conv_state_roll_tail(conv_tail, conv_state, B, T, L->conv_dim, stream));
     GDN_CUDA(stage_mark(L, 2, stream));
     ChunkArgs ca;
-    ca.qkv = qkv; ca.qkv_ld = L->conv_dim;
+    ca.qkv = proj; ca.qkv_ld = L->proj_ld;
     ca.proj = proj; ca.proj_ld = L->proj_ld;
     ca.z_off = z_off; ca.a_off = a_off; ca.b_off = b_off;
     ca.a_log = L->a_log; ca.dt_bias = L->dt_bias; ca.norm_w = L->norm_w; ca.eps = L->dims.eps;
@@ -369,7 +383,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     eo.out = out;
     eo.ld = h;
     eo.b_tiled = L->w_out;
-    GDN_CUDA(gemm_bf16_tn(y, L->vd, L->w_out, L->vd, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, 1, stream, true));
+    GDN_CUDA(gemm_bf16_persistent(y, L->vd, L->w_out, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, stream, true));
     GDN_CUDA(stage_mark(L, 5, stream));
   }
   if (L->tp_size > 1 && comm) {

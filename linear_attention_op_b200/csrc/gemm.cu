@@ -510,6 +510,337 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
 }
 
 // ---------------------------------------------------------------------------------------------
+// Persistent 128 x 256 GEMM for the prefill projections
+// ---------------------------------------------------------------------------------------------
+// One CTA per SM walks the tiles blockIdx.x, + gridDim.x, ... in grouped raster order.  TMEM holds two
+// 128 x 256 fp32 accumulators (all 512 columns): warp 1 issues the MMAs of the next tile into one while
+// the epilogue warps drain the other, and warp 0 keeps the 4-stage ring full across tile boundaries.
+//
+// kEpiPrefillInProj fuses the causal conv (K = 4) + SiLU of the conv channels into the epilogue.  Its
+// M tiles advance by 125 rows and start 3 rows early, so every output row finds its 3 predecessors in
+// the same tile (tile rows 0..2 are recomputed halo and never stored; 2.4% extra MMA work instead of a
+// separate conv pass over HBM).  A row's predecessors sit in the 3 lanes below it (warp shuffles);
+// lanes 0..2 of lane quarters 1..3 take them from the previous quarter's warp through shared memory.
+// Eight epilogue warps (two per TMEM lane quarter, one per 128-column half) keep enough warps issuing
+// to hide the epilogue behind the next tile's MMAs.  Predecessors before
+// the start of a sequence come from conv_state (9B/kernels/layer_reader.cpp:103-124: the conv window
+// continues the cached history); the raw last 3 inputs of each sequence go to conv_tail, from which
+// conv_state_roll_tail() rolls the state after the kernel.
+constexpr int kPBN = 256;
+constexpr int kPStages = 4;
+constexpr int kConvHalo = 3;
+using PCfg = GemmCfg<kPBN, kPStages>;
+constexpr int kPEpiWarps = 8;  // two per TMEM lane quarter, each draining one 128-column half of a tile
+constexpr int kPThreads = 64 + 32 * kPEpiWarps;
+constexpr int kPXchOffset = PCfg::kBarOffset + 256;
+constexpr int kPSmemBytes = kPXchOffset + 2 * 2 * 4 * 48 * 4 + 1024;
+static_assert(kPSmemBytes <= 227 * 1024, "persistent GEMM shared memory");
+
+// Named barriers: id 1 + half over the 4 epilogue warps of one column half (conv exchange), id 3 over
+// all 8 epilogue warps (per-tile vote); 0 is __syncthreads.
+__device__ __forceinline__ void epi_half_sync(int half) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
+}
+__device__ __forceinline__ bool epi_bar_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 3, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void store_f32x16(float* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+// Conv epilogue of one 16-column chunk (columns n0 .. n0 + 15, all conv channels) for tile row r = 32 q +
+// lane, output row `row` (stored when `store`).  xw: this warp's exchange slot, xp: the previous warp's.
+__device__ __forceinline__ void conv_chunk(const GemmEpiArgs& ep, const float (&v)[16], int q, int half, int lane,
+                                           int row, bool store, int n0, float* xw, const float* xp) {
+  if (lane >= 32 - kConvHalo) store_f32x16(xw + (lane - (32 - kConvHalo)) * 16, v);
+  epi_half_sync(half);
+  // h1/h2/h3 = inputs at t - 1, t - 2, t - 3.  Predecessor j of lane l < j is lane 32 - j + l of the
+  // previous warp, i.e. exchange row 3 - j + l.
+  float h1[16], h2[16], h3[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    h1[j] = __shfl_up_sync(0xffffffffu, v[j], 1);
+    h2[j] = __shfl_up_sync(0xffffffffu, v[j], 2);
+    h3[j] = __shfl_up_sync(0xffffffffu, v[j], 3);
+  }
+  if (q > 0 && lane < kConvHalo) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (lane < 1) h1[j] = xp[(2 + lane) * 16 + j];
+      if (lane < 2) h2[j] = xp[(1 + lane) * 16 + j];
+      h3[j] = xp[lane * 16 + j];
+    }
+  }
+  if (!store) return;
+  const int cr = ep.conv_rows, T = ep.seq_len;
+  const int b = row / T, t = row - b * T;
+  if (t < kConvHalo) {
+    // Taps before the sequence start: conv_state row 3 + t - j holds the input at time t - j.
+    const float* cs = ep.conv_state + static_cast<int64_t>(b) * 3 * cr + n0;
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      if (t < 1) {
+        const float4 x = *reinterpret_cast<const float4*>(cs + static_cast<int64_t>(2 + t) * cr + j);
+        h1[j] = x.x; h1[j + 1] = x.y; h1[j + 2] = x.z; h1[j + 3] = x.w;
+      }
+      if (t < 2) {
+        const float4 x = *reinterpret_cast<const float4*>(cs + static_cast<int64_t>(1 + t) * cr + j);
+        h2[j] = x.x; h2[j + 1] = x.y; h2[j + 2] = x.z; h2[j + 3] = x.w;
+      }
+      const float4 x = *reinterpret_cast<const float4*>(cs + static_cast<int64_t>(t) * cr + j);
+      h3[j] = x.x; h3[j + 1] = x.y; h3[j + 2] = x.z; h3[j + 3] = x.w;
+    }
+  }
+  if (t >= T - kConvHalo) {
+    float* tl = ep.conv_tail + (static_cast<int64_t>(b) * 3 + (t - T + 3)) * cr + n0;
+    store_f32x16(tl, v);
+  }
+  float y[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(ep.conv_w) + n0 + j);
+    y[j] = silu_fast(w.x * h3[j] + w.y * h2[j] + w.z * h1[j] + w.w * v[j]);
+  }
+  store_f32x16(static_cast<float*>(ep.out) + static_cast<int64_t>(row) * ep.ld + n0, y);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, int M, int N, int K, int m_stride,
+                           int m_tiles, int n_tiles, int group_m, const uint8_t* b_tiled, GemmEpiArgs ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPStages * PCfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PCfg::kBarOffset);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* xch = reinterpret_cast<float*>(smem + kPXchOffset);  // [2 halves][2 chunk parities][4 quarters][3][16]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int halo = kBM - m_stride;
+  const int tiles = m_tiles * n_tiles;
+  const int kblocks = (K + kBK - 1) / kBK;
+  const int per_group = group_m * n_tiles;
+  auto coords = [&](int t, int& mt, int& nt) {
+    const int first_m = (t / per_group) * group_m;
+    const int gsize = min(m_tiles - first_m, group_m);
+    mt = first_m + (t % per_group) % gsize;
+    nt = (t % per_group) / gsize;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kPEpiWarps);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kPBN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      const uint64_t pol = policy_evict_last();
+      auto load_a = [&](int s, int mt, int kb) {
+        tma_load_2d(sA + s * PCfg::kABytes, &tmA, &full[s], kb * kBK, mt * m_stride - halo, pol);
+      };
+      auto load_b = [&](int s, int nt, int kb) {
+#pragma unroll
+        for (int h = 0; h < kPBN / 128; ++h)
+          bulk_load_hint(sB + s * PCfg::kBBytes + h * 16384,
+                         b_tiled + (static_cast<int64_t>(nt * (kPBN / 128) + h) * kblocks + kb) * 16384, 16384,
+                         &full[s], pol);
+      };
+      // The weights do not depend on the previous kernel: the first stages of the first tile's B are
+      // requested before waiting for it.
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < tiles) {
+        int mt, nt;
+        coords(blockIdx.x, mt, nt);
+        pre = min(kblocks, kPStages);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], PCfg::kStageBytes);
+          load_b(i, nt, i);
+        }
+      }
+      griddep_wait();
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        int mt, nt;
+        coords(t, mt, nt);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % kPStages);
+          if (static_cast<int>(it) < pre) {
+            load_a(s, mt, kb);
+            continue;
+          }
+          if (!mbar_wait(&empty[s], ((it / kPStages) & 1) ^ 1, kErrWaitSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], PCfg::kStageBytes);
+          load_a(s, mt, kb);
+          load_b(s, nt, kb);
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA exits.
+        for (uint32_t j = it; j > 0 && j + kPStages > it; --j)
+          mbar_wait(&full[(j - 1) % kPStages], ((j - 1) / kPStages) & 1, kErrWaitTmaFull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_dense(1, kBM, kPBN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++local) {
+        const int a = local & 1;
+        if (!mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(a * kPBN);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = static_cast<int>(it % kPStages);
+          if (!mbar_wait(&full[s], (it / kPStages) & 1, kErrWaitTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sdesc_k_sw128(smem_u32(sA + s * PCfg::kABytes));
+          const uint64_t db = sdesc_k_sw128(smem_u32(sB + s * PCfg::kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[a]);
+      }
+    }
+    __syncwarp();
+  } else {
+    griddep_wait();  // the epilogue writes buffers the previous kernel may still read
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // column half [128 half, +128) of each tile
+    const int r = q * 32 + lane;
+    ConvHist unused;
+    int local = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const int a = local & 1;
+      const bool ok = mbar_wait(&acc_full[a], (local >> 1) & 1, kErrWaitAccum);
+      if (epi_bar_any(!ok)) break;  // every epilogue warp leaves together
+      tc_fence_after();
+      int mt, nt;
+      coords(t, mt, nt);
+      const int row = mt * m_stride - halo + r;
+      const bool store = r >= halo && row < M;
+      const uint32_t t_row = tmem + static_cast<uint32_t>(a * kPBN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int c0 = half * (kPBN / 2); c0 < (half + 1) * (kPBN / 2); c0 += 16) {
+        float v[16];
+        tmem_ld16(t_row + c0, v);
+        const int n0 = nt * kPBN + c0;
+        if constexpr (EPI == kEpiPrefillInProj) {
+          if (n0 < ep.conv_rows) {
+            float* xs = xch + (half * 2 + ((c0 >> 4) & 1)) * 4 * 48;
+            conv_chunk(ep, v, q, half, lane, row, store, n0, xs + q * 48, xs + (q > 0 ? q - 1 : 0) * 48);
+            continue;
+          }
+          epilogue16<kEpiStoreF32>(ep, store ? row : M, n0, M, N, v, unused);
+        } else {
+          epilogue16<EPI>(ep, store ? row : M, n0, M, N, v, unused);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 2 * kPBN);
+}
+
+template <int EPI>
+static cudaError_t launch_persistent(const CUtensorMap& ta, const void* b_tiled, int M, int N, int K, int m_stride,
+                                     const GemmEpiArgs& ep, bool pdl, cudaStream_t stream) {
+  auto kern = gemm_persistent_kernel<EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int m_tiles = (M + m_stride - 1) / m_stride;
+  const int n_tiles = (N + kPBN - 1) / kPBN;
+  const int tiles = m_tiles * n_tiles;
+  const int group_m = std::min(16, m_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min(tiles, sms)));
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = kPSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kern, ta, M, N, K, m_stride, m_tiles, n_tiles, group_m,
+                            static_cast<const uint8_t*>(b_tiled), ep);
+}
+
+cudaError_t gemm_bf16_persistent(const void* A, int64_t lda, const void* B_tiled, int M, int N, int K, int epi,
+                                 const GemmEpiArgs& ep, cudaStream_t stream, bool pdl) {
+  if (M <= 0 || N <= 0 || K <= 0 || (K & 7) || !B_tiled || !ep.out) return cudaErrorInvalidValue;
+  CUtensorMap ta;
+  std::memset(&ta, 0, sizeof(ta));
+  cudaError_t e = make_tmap(&ta, A, M, K, lda, kBM);
+  if (e != cudaSuccess) return e;
+  switch (epi) {
+    case kEpiStoreF32: return launch_persistent<kEpiStoreF32>(ta, B_tiled, M, N, K, kBM, ep, pdl, stream);
+    case kEpiStoreBF16: return launch_persistent<kEpiStoreBF16>(ta, B_tiled, M, N, K, kBM, ep, pdl, stream);
+    case kEpiPrefillInProj:
+      if (ep.seq_len <= 0 || ep.conv_rows <= 0 || (ep.conv_rows & 15) || ep.conv_rows > N || (ep.ld & 3) ||
+          (M % ep.seq_len) || !ep.conv_w || !ep.conv_state || !ep.conv_tail ||
+          (reinterpret_cast<uintptr_t>(ep.out) & 15) || (reinterpret_cast<uintptr_t>(ep.conv_state) & 15) ||
+          (reinterpret_cast<uintptr_t>(ep.conv_tail) & 15) || (reinterpret_cast<uintptr_t>(ep.conv_w) & 15))
+        return cudaErrorInvalidValue;
+      return launch_persistent<kEpiPrefillInProj>(ta, B_tiled, M, N, K, kBM - kConvHalo, ep, pdl, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Pre-tiled weights
 // ---------------------------------------------------------------------------------------------
 size_t tiled_weight_bytes(int rows, int cols) {

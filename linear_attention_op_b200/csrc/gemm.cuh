@@ -17,6 +17,9 @@ enum GemmEpi : int {
                          //   rows [conv_rows, conv_rows + z_rows): plain
                          //   next nheads rows: g = -exp(A_log) softplus(a + dt_bias)
                          //   next nheads rows: beta = sigmoid(b)
+  kEpiPrefillInProj = 5, // row-major fp32 store of the prefill in_proj (rows = tokens of seq_len-token
+                         // sequences); columns [0, conv_rows) get the causal conv (K = 4) + SiLU, the
+                         // raw last 3 inputs of each sequence go to conv_tail (persistent kernel only)
 };
 
 struct GemmEpiArgs {
@@ -30,6 +33,9 @@ struct GemmEpiArgs {
   float* conv_state = nullptr;    // [N, 3, conv_rows] (N = number of sequences = GEMM N)
   const float* a_log = nullptr;   // [nheads]
   const float* dt_bias = nullptr; // [nheads]
+  // kEpiPrefillInProj only (also uses conv_rows, conv_w; conv_state is read, not written)
+  int seq_len = 0;
+  float* conv_tail = nullptr;     // [M / seq_len, 3, conv_rows]: raw inputs at times seq_len - 3 .. - 1
   // Operands stored pre-tiled by tile_weights_bf16 (then A / B must equal these pointers; lda / ldb unused).
   const void* a_tiled = nullptr;
   const void* b_tiled = nullptr;
@@ -47,6 +53,13 @@ struct GemmEpiArgs {
 cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
                          const GemmEpiArgs& args, int ksplit, cudaStream_t stream, bool pdl = false,
                          bool trigger = false);
+
+// Persistent variant for the large prefill projections: one CTA per SM, 128 x 256 tiles, two TMEM
+// accumulators so a tile's epilogue overlaps the next tile's MMAs.  A [M, K] bf16 row-major (row stride
+// lda); B_tiled = weights [N, K] pre-tiled by tile_weights_bf16.  epi: kEpiStoreF32, kEpiStoreBF16 or
+// kEpiPrefillInProj.
+cudaError_t gemm_bf16_persistent(const void* A, int64_t lda, const void* B_tiled, int M, int N, int K, int epi,
+                                 const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false);
 
 // Weights kept in the GEMM's streaming layout: [ceil(rows/128), rounded up to even][cols/64] blocks of
 // 16 KB, each block the 128B-swizzled shared-memory image of a 128 x 64 bf16 tile, so that a K-slice of

@@ -41,10 +41,10 @@ struct RecurrenceArgs {
 // pdl: may start while the previous kernel (the in_proj GEMM) runs; it loads the state first.
 cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream, bool pdl = false);
 
-// Prefill causal conv (K = 4) + SiLU: in[row * in_ld + c] pre-conv channels c < C, out[row * out_ld + c].
-// conv_state [B, 3, C] supplies the history before t = 0 and is then rolled to the last 3 inputs.
-cudaError_t conv_prefill(const float* in, int64_t in_ld, float* out, int64_t out_ld, const float* conv_w,
-                         float* conv_state, int B, int T, int C, cudaStream_t stream);
+// Conv-state roll after the prefill in_proj (whose epilogue ran the conv): conv_state [B, 3, C] row j
+// becomes the input at time T - 3 + j, read from tail [B, 3, C] (the raw inputs at T - 3 .. T - 1) or,
+// for times before 0, from the old state.
+cudaError_t conv_state_roll_tail(const float* tail, float* conv_state, int B, int T, int C, cudaStream_t stream);
 
 // Chunked prefill of the whole recurrence + gated RMSNorm over the layer's in_proj output.
 struct ChunkArgs {

@@ -24,6 +24,7 @@ enum DeviceError : int {
   kErrWaitTmaFull = 0x101,     // MMA issuer timed out waiting for a TMA stage
   kErrWaitSmemEmpty = 0x102,   // TMA producer timed out waiting for a free stage
   kErrWaitAccum = 0x103,       // epilogue timed out waiting for the accumulator
+  kErrWaitAccEmpty = 0x104,    // MMA issuer timed out waiting for the epilogue to free an accumulator
   kErrBadArgs = 0x201,         // kernel saw arguments the host should have rejected
 };
 
