@@ -498,8 +498,22 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   cudaError_t e = cudaSuccess;
   if (!ep.a_tiled && (e = make_tmap(&ta, A, M, K, lda, kBM)) != cudaSuccess) return e;
   if (!ep.b_tiled && (e = make_tmap(&tb, B, N, K, ldb, BN)) != cudaSuccess) return e;
-  // Skinny (decode) tiles use a 3-stage ring (< 75 KB) so three CTAs share an SM and a split-K launch fits
-  // in one wave of clusters; wide tiles take the whole SM.
+  // Skinny tiles whose A operand is a pre-tiled weight matrix (the decode projections) stream that matrix
+  // from HBM: one CTA per SM with an 8-stage ring (up to 192 KB in flight per SM), split-K only as far as
+  // the whole launch stays one wave, so no CTA waits for another to finish before it starts streaming.
+  // Other skinny tiles use a 3-stage ring (< 75 KB) so three CTAs share an SM; wide tiles take the SM.
+  if (ep.a_tiled && BN <= 64) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+    if (ksplit <= 0) ksplit = std::max(1, std::min(8, sms / tiles));
+    switch (BN) {
+      case 16: return dispatch_epi<16, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+      case 32: return dispatch_epi<32, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+      default: return dispatch_epi<64, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    }
+  }
   switch (BN) {
     case 16: return dispatch_epi<16, 3>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
     case 32: return dispatch_epi<32, 3>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
