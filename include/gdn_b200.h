@@ -90,7 +90,8 @@ typedef struct gdn_comm gdn_comm;   /* opaque: a NCCL communicator over the tens
 
 /* Build a layer handle for tensor-parallel rank `tp_rank` of `tp_size` (1 = single GPU), on the current
  * CUDA device.  Rank r owns k-heads [r*Hk/G, (r+1)*Hk/G) and v-heads [r*Hv/G, (r+1)*Hv/G): in_proj rows
- * of those heads, out_proj columns of those v-heads.  Replaces Qwen35GatedDeltaNetTT.__init__
+ * of those heads, out_proj columns of those v-heads.  Hv/Hk above 8 returns GDN_ERR_UNSUPPORTED (the
+ * Qwen3.5 layers use 1 and 2).  Replaces Qwen35GatedDeltaNetTT.__init__
  * (9B/gdn_layer.py:55-78) and Qwen35_08B_GDNStackL1's per-layer _Layer (0.8B/gdn_l1.py:91-130). */
 GDN_API gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* weights, int32_t tp_rank, int32_t tp_size,
                             gdn_layer** out_layer);

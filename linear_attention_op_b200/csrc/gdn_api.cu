@@ -172,6 +172,9 @@ extern "C" gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* 
   if (d.num_k_heads <= 0 || d.num_v_heads <= 0 || d.num_v_heads % d.num_k_heads)
     return fail(GDN_ERR_INVALID_ARGUMENT, "num_v_heads %d must be a multiple of num_k_heads %d", d.num_v_heads,
                 d.num_k_heads);
+  if (d.num_v_heads / d.num_k_heads > 8)
+    return fail(GDN_ERR_UNSUPPORTED, "%d v-heads per k-head unsupported (at most 8: one thread-block cluster)",
+                d.num_v_heads / d.num_k_heads);
   if (!(d.eps > 0.f)) return fail(GDN_ERR_INVALID_ARGUMENT, "eps must be > 0");
   if (tp_size <= 0 || tp_rank < 0 || tp_rank >= tp_size)
     return fail(GDN_ERR_INVALID_ARGUMENT, "tp_rank %d / tp_size %d", tp_rank, tp_size);
@@ -288,6 +291,59 @@ extern "C" gdn_status gdn_layer_set_stage_events(gdn_layer* L, void* const* even
   return GDN_OK;
 }
 
+// One decode step (T = 1): in_proj (weights as the 128-row operand, gating fused into the epilogue) ->
+// conv + conv-state roll + gated delta rule + gated RMSNorm (decode_step_kernel, which loads the state
+// and the conv history while the GEMM runs) -> out_proj, chained by programmatic dependent launch.
+// proj [B, proj_ld] fp32 and y [B, vd] bf16 are scratch.
+static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* rec_state, float* conv_state,
+                               float* proj, __nv_bfloat16* y, uint16_t* out, cudaStream_t stream, bool marks) {
+  const int h = L->dims.hidden;
+  const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
+  GemmEpiArgs ep;
+  ep.a_tiled = L->w_in;
+  ep.out = proj;
+  ep.ld = L->proj_ld;
+  ep.conv_rows = L->conv_dim;
+  ep.z_rows = L->vd;
+  ep.nheads = L->hv;
+  ep.a_log = L->a_log;
+  ep.dt_bias = L->dt_bias;
+  GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
+  if (marks) {
+    GDN_CUDA(stage_mark(L, 1, stream));
+    GDN_CUDA(stage_mark(L, 2, stream));
+    GDN_CUDA(stage_mark(L, 3, stream));
+  }
+  RecurrenceArgs ra;
+  ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
+  ra.k = proj + L->kd; ra.k_tok = L->proj_ld; ra.k_head = kHeadDim;
+  ra.v = proj + 2 * L->kd; ra.v_tok = L->proj_ld; ra.v_head = kHeadDim;
+  ra.z = proj + z_off; ra.z_tok = L->proj_ld; ra.z_head = kHeadDim;
+  ra.g = proj + a_off; ra.g_tok = L->proj_ld; ra.g_head = 1;
+  ra.beta = proj + b_off; ra.b_tok = L->proj_ld; ra.b_head = 1;
+  ra.norm_w = L->norm_w;
+  ra.eps = L->dims.eps;
+  ra.y = y; ra.y_tok = L->vd; ra.y_head = kHeadDim;
+  ra.state = rec_state;
+  ra.B = B; ra.T = 1; ra.Hk = L->hk; ra.Hv = L->hv;
+  ra.scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
+  ra.l2norm = 1;
+  ra.conv_w = L->conv_w;
+  ra.conv_state = conv_state;
+  ra.conv_dim = L->conv_dim;
+  ra.k_conv = L->kd;
+  ra.v_conv = 2 * L->kd;
+  GDN_CUDA(decode_step_forward(ra, stream));
+  if (marks) GDN_CUDA(stage_mark(L, 4, stream));
+  GemmEpiArgs eo;
+  eo.out = out;
+  eo.ld = h;
+  eo.a_tiled = L->w_out;
+  GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
+  if (marks) GDN_CUDA(stage_mark(L, 5, stream));
+  return GDN_OK;
+}
+
 extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t B, int32_t T, float* rec_state,
                                         float* conv_state, uint16_t* out, gdn_comm* comm, void* stream_ptr) {
   if (!L || !x || !rec_state || !conv_state || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_forward: null argument");
@@ -315,44 +371,8 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
 
   GDN_CUDA(stage_mark(L, 0, stream));
   if (T == 1) {
-    // ---- decode: in_proj (weights as the 128-row operand) with conv + gating fused into the epilogue
-    GemmEpiArgs ep;
-    ep.a_tiled = L->w_in;
-    ep.out = proj;
-    ep.ld = L->proj_ld;
-    ep.conv_rows = L->conv_dim;
-    ep.z_rows = L->vd;
-    ep.nheads = L->hv;
-    ep.conv_w = L->conv_w;
-    ep.conv_state = conv_state;
-    ep.a_log = L->a_log;
-    ep.dt_bias = L->dt_bias;
-    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
-    GDN_CUDA(stage_mark(L, 1, stream));
-    GDN_CUDA(stage_mark(L, 2, stream));
-    GDN_CUDA(stage_mark(L, 3, stream));
-    RecurrenceArgs ra;
-    ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
-    ra.k = proj + L->kd; ra.k_tok = L->proj_ld; ra.k_head = kHeadDim;
-    ra.v = proj + 2 * L->kd; ra.v_tok = L->proj_ld; ra.v_head = kHeadDim;
-    ra.z = proj + z_off; ra.z_tok = L->proj_ld; ra.z_head = kHeadDim;
-    ra.g = proj + a_off; ra.g_tok = L->proj_ld; ra.g_head = 1;
-    ra.beta = proj + b_off; ra.b_tok = L->proj_ld; ra.b_head = 1;
-    ra.norm_w = L->norm_w;
-    ra.eps = L->dims.eps;
-    ra.y = y; ra.y_tok = L->vd; ra.y_head = kHeadDim;
-    ra.state = rec_state;
-    ra.B = B; ra.T = 1; ra.Hk = L->hk; ra.Hv = L->hv;
-    ra.scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
-    ra.l2norm = 1;
-    GDN_CUDA(recurrence_forward(ra, stream, true));
-    GDN_CUDA(stage_mark(L, 4, stream));
-    GemmEpiArgs eo;
-    eo.out = out;
-    eo.ld = h;
-    eo.a_tiled = L->w_out;
-    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
-    GDN_CUDA(stage_mark(L, 5, stream));
+    gdn_status ds = decode_chain(L, x, B, rec_state, conv_state, proj, y, out, stream, true);
+    if (ds != GDN_OK) return ds;
   } else {
     // ---- prefill: in_proj with the causal conv + SiLU fused into its epilogue -> conv-state roll ->
     //      chunked recurrence + gated RMSNorm -> out_proj
@@ -452,40 +472,7 @@ extern "C" gdn_status gdn_layer_decode_static(gdn_layer* L, const uint16_t* x, i
   const int h = L->dims.hidden;
   float* proj = static_cast<float*>(base);
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(base) + proj_bytes);
-  const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
-  GemmEpiArgs ep;
-  ep.out = proj;
-  ep.ld = L->proj_ld;
-  ep.conv_rows = L->conv_dim;
-  ep.z_rows = L->vd;
-  ep.nheads = L->hv;
-  ep.conv_w = L->conv_w;
-  ep.conv_state = conv_state;
-  ep.a_log = L->a_log;
-  ep.dt_bias = L->dt_bias;
-  ep.a_tiled = L->w_in;
-  GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream));
-  RecurrenceArgs ra;
-  ra.q = proj; ra.q_tok = L->proj_ld; ra.q_head = kHeadDim;
-  ra.k = proj + L->kd; ra.k_tok = L->proj_ld; ra.k_head = kHeadDim;
-  ra.v = proj + 2 * L->kd; ra.v_tok = L->proj_ld; ra.v_head = kHeadDim;
-  ra.z = proj + z_off; ra.z_tok = L->proj_ld; ra.z_head = kHeadDim;
-  ra.g = proj + a_off; ra.g_tok = L->proj_ld; ra.g_head = 1;
-  ra.beta = proj + b_off; ra.b_tok = L->proj_ld; ra.b_head = 1;
-  ra.norm_w = L->norm_w;
-  ra.eps = L->dims.eps;
-  ra.y = y; ra.y_tok = L->vd; ra.y_head = kHeadDim;
-  ra.state = rec_state;
-  ra.B = B; ra.T = 1; ra.Hk = L->hk; ra.Hv = L->hv;
-  ra.scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
-  ra.l2norm = 1;
-  GDN_CUDA(recurrence_forward(ra, stream));
-  GemmEpiArgs eo;
-  eo.out = out;
-  eo.ld = h;
-  eo.a_tiled = L->w_out;
-  GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream));
-  return GDN_OK;
+  return decode_chain(L, x, B, rec_state, conv_state, proj, y, out, stream, false);
 }
 
 extern "C" gdn_status gdn_recurrence_forward(const float* q, const float* k, const float* v, const float* g,

@@ -47,27 +47,9 @@ struct GemmCfg {
   static_assert(BN * kBM * 4 <= STAGES * kStageBytes, "split-K partial tile must fit in the stage ring");
 };
 
-// Conv history of row m (a conv channel) for tokens n0 .. n0 + 15: conv_state rows 0..2, oldest first.
-struct ConvHist {
-  float h[3][16];
-};
-
-__device__ __forceinline__ void conv_prefetch(const GemmEpiArgs& ep, int m, int n0, int N, ConvHist& hs) {
-  const int cr = ep.conv_rows;
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int n = n0 + j;
-    const float* cs = ep.conv_state + static_cast<int64_t>(n < N ? n : 0) * 3 * cr + m;
-    hs.h[0][j] = cs[0];
-    hs.h[1][j] = cs[cr];
-    hs.h[2][j] = cs[2 * cr];
-  }
-}
-
-// For kEpiDecodeInProj conv rows `hs` must hold the conv history of (m, n0 .. n0 + 15) (conv_prefetch).
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0, int M, int N,
-                                           const float (&v)[16], const ConvHist& hs) {
+                                           const float (&v)[16]) {
   if (m >= M) return;
   if constexpr (EPI == kEpiStoreF32) {
     float* row = static_cast<float*>(ep.out) + static_cast<int64_t>(m) * ep.ld + n0;
@@ -110,24 +92,7 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
   } else {  // kEpiDecodeInProj
     float* out = static_cast<float*>(ep.out);
     const int cr = ep.conv_rows;
-    if (m < cr) {
-      // Causal conv over the last 3 inputs (conv_state rows 0..2, oldest first) and this token; the
-      // state rolls by one (9B/kernels/layer_reader.cpp:184-197; HF torch_causal_conv1d_update).  All 48
-      // history loads are issued before any store so their latencies overlap.
-      const float4 w = *reinterpret_cast<const float4*>(ep.conv_w + static_cast<int64_t>(m) * 4);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = n0 + j;
-        if (n < N) {
-          float* cs = ep.conv_state + static_cast<int64_t>(n) * 3 * cr + m;
-          cs[0] = hs.h[1][j];
-          cs[cr] = hs.h[2][j];
-          cs[2 * cr] = v[j];
-          out[static_cast<int64_t>(n) * ep.ld + m] =
-              silu_f(w.x * hs.h[0][j] + w.y * hs.h[1][j] + w.z * hs.h[2][j] + w.w * v[j]);
-        }
-      }
-    } else if (m < cr + ep.z_rows) {
+    if (m < cr + ep.z_rows) {  // conv rows (raw: the conv runs in the decode step kernel) and z rows
 #pragma unroll
       for (int j = 0; j < 16; ++j)
         if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = v[j];
@@ -270,15 +235,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int r = q * 32 + lane;     // row inside the tile
   const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
   const bool epi_warp = warp >= 2;
-  // The decode in_proj epilogue reads the conv history of its first column chunk while the main loop runs.
-  ConvHist hist;
-  const int first_c0 = ksplit > 1 ? split * 16 : 0;
   if (epi_warp) {
     griddep_wait();  // the epilogue writes buffers the previous kernel may still read
-    if constexpr (EPI == kEpiDecodeInProj) {
-      const int m = m_tile * kBM + r;
-      if (m < M && m < ep.conv_rows && first_c0 < BN) conv_prefetch(ep, m, n_tile * BN + first_c0, N, hist);
-    }
     mbar_wait(accum, 0, kErrWaitAccum);
     tc_fence_after();
   }
@@ -289,9 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(t_row + c0, v);
-        if constexpr (EPI == kEpiDecodeInProj)
-          if (c0 != first_c0 && m < M && m < ep.conv_rows) conv_prefetch(ep, m, n_tile * BN + c0, N, hist);
-        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v, hist);
+        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
       }
     }
   } else {
@@ -335,9 +291,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        if constexpr (EPI == kEpiDecodeInProj)
-          if (c0 != first_c0 && m < M && m < ep.conv_rows) conv_prefetch(ep, m, n_tile * BN + c0, N, hist);
-        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v, hist);
+        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
       }
     }
     __syncwarp();
@@ -765,7 +719,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;   // column half [128 half, +128) of each tile
     const int r = q * 32 + lane;
-    ConvHist unused;
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -788,9 +741,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
             conv_chunk(ep, v, q, half, lane, row, store, n0, xs + q * 48, xs + (q > 0 ? q - 1 : 0) * 48);
             continue;
           }
-          epilogue16<kEpiStoreF32>(ep, store ? row : M, n0, M, N, v, unused);
+          epilogue16<kEpiStoreF32>(ep, store ? row : M, n0, M, N, v);
         } else {
-          epilogue16<EPI>(ep, store ? row : M, n0, M, N, v, unused);
+          epilogue16<EPI>(ep, store ? row : M, n0, M, N, v);
         }
       }
       tc_fence_before();

@@ -13,8 +13,7 @@ enum GemmEpi : int {
   kEpiStoreF32T = 2,     // out[n * ld + m] = acc          (A = weights, B = activations)
   kEpiStoreBF16T = 3,    // out[n * ld + m] = bf16(acc)
   kEpiDecodeInProj = 4,  // transposed store of the fused in_proj of one decode token per sequence:
-                         //   rows [0, conv_rows): causal conv (K = 4) + SiLU, rolls conv_state
-                         //   rows [conv_rows, conv_rows + z_rows): plain
+                         //   rows [0, conv_rows + z_rows): plain (the conv runs in the decode step kernel)
                          //   next nheads rows: g = -exp(A_log) softplus(a + dt_bias)
                          //   next nheads rows: beta = sigmoid(b)
   kEpiPrefillInProj = 5, // row-major fp32 store of the prefill in_proj (rows = tokens of seq_len-token
@@ -25,15 +24,16 @@ enum GemmEpi : int {
 struct GemmEpiArgs {
   void* out = nullptr;
   int64_t ld = 0;  // leading dimension of `out`, in elements
-  // kEpiDecodeInProj only
+  // kEpiDecodeInProj and kEpiPrefillInProj
   int conv_rows = 0;
+  // kEpiDecodeInProj only
   int z_rows = 0;
   int nheads = 0;
-  const float* conv_w = nullptr;  // [conv_rows, 4]
-  float* conv_state = nullptr;    // [N, 3, conv_rows] (N = number of sequences = GEMM N)
   const float* a_log = nullptr;   // [nheads]
   const float* dt_bias = nullptr; // [nheads]
-  // kEpiPrefillInProj only (also uses conv_rows, conv_w; conv_state is read, not written)
+  // kEpiPrefillInProj only
+  const float* conv_w = nullptr;  // [conv_rows, 4]
+  const float* conv_state = nullptr;  // [M / seq_len, 3, conv_rows], read (the roll runs after the GEMM)
   int seq_len = 0;
   float* conv_tail = nullptr;     // [M / seq_len, 3, conv_rows]: raw inputs at times seq_len - 3 .. - 1
   // Operands stored pre-tiled by tile_weights_bf16 (then A / B must equal these pointers; lda / ldb unused).

@@ -35,11 +35,24 @@ struct RecurrenceArgs {
   int B = 0, T = 0, Hk = 0, Hv = 0;
   float scale = 0.0f;  // q scale (dk^-0.5 by default)
   int l2norm = 1;
+  // Layer decode only (decode_step_forward): q, k, v above are the raw in_proj outputs of the conv
+  // channels; channel index (into conv_w / conv_state) of q element (kh, i) is kh * 128 + i, of k element
+  // k_conv + kh * 128 + i, of v element v_conv + h * 128 + i.
+  const float* conv_w = nullptr;  // [conv_dim, 4]
+  float* conv_state = nullptr;    // [B, 3, conv_dim], rolled in place
+  int conv_dim = 0;
+  int k_conv = 0, v_conv = 0;
 };
 
 // Token-by-token gated delta rule, one CTA per (sequence, v-head), state kept in registers.
 // pdl: may start while the previous kernel (the in_proj GEMM) runs; it loads the state first.
 cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream, bool pdl = false);
+
+// Layer decode step (T = 1): causal conv + SiLU of q, k, v with the conv-state roll, then the gated delta
+// rule and the gated RMSNorm.  One CTA per (sequence, v-head); the v-heads of a GQA group (at most 8) form
+// a thread-block cluster so that exactly one of them rolls the shared q/k conv state after all have read
+// it.  Launched with programmatic dependent launch after the in_proj GEMM.
+cudaError_t decode_step_forward(const RecurrenceArgs& a, cudaStream_t stream);
 
 // Conv-state roll after the prefill in_proj (whose epilogue ran the conv): conv_state [B, 3, C] row j
 // becomes the input at time T - 3 + j, read from tail [B, 3, C] (the raw inputs at T - 3 .. T - 1) or,

@@ -153,4 +153,209 @@ cudaError_t recurrence_forward(const RecurrenceArgs& a, cudaStream_t stream, boo
   return cudaLaunchKernelEx(&cfg, recurrence_kernel, a);
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Layer decode step with the causal conv fused
+// ---------------------------------------------------------------------------------------------
+// One CTA per (sequence b, v-head h), as recurrence_kernel, with the causal conv (K = 4) + SiLU of its
+// q, k and v channels and the conv-state roll (9B/kernels/layer_reader.cpp:184-197; HF
+// torch_causal_conv1d_update).  The v-heads of one GQA group share the q/k channels of their k-head, so
+// they run as one thread-block cluster: every CTA reads the q/k history, arrives on the cluster barrier,
+// and only cluster rank 0 rolls the q/k state after the barrier, once every sibling has read it.  Before
+// waiting for the in_proj GEMM each CTA loads its recurrent state, the conv history and the conv weights
+// (cp.async into shared memory), all of which that kernel leaves untouched.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+constexpr int kStepCh = 3 * kHeadDim;  // q, k, v channels of one CTA
+
+__global__ void __launch_bounds__(kRecThreads, 2) decode_step_kernel(RecurrenceArgs a) {
+  const int b = blockIdx.x / a.Hv, h = blockIdx.x % a.Hv;
+  const int ratio = a.Hv / a.Hk, kh = h / ratio;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = lane * 4, r0 = warp * 16;
+
+  __shared__ __align__(16) float4 s_w[kStepCh];  // conv taps of each channel
+  __shared__ float s_hist[3][kStepCh];           // conv history, oldest first
+  __shared__ __align__(16) float s_q[kHeadDim], s_k[kHeadDim], s_v[kHeadDim], s_z[kHeadDim];
+  __shared__ __align__(16) float s_u[kHeadDim], s_o[kHeadDim];
+  __shared__ float4 s_rk[8][32], s_rq[8][32];
+  __shared__ float s_red[4][4];
+  __shared__ float s_scal[2];
+
+  griddep_launch_dependents();  // the successor (out_proj) reads y only after waiting for this kernel
+  // CTA-local channel idx -> conv channel: q (0..127), k (128..255), v (256..383)
+  auto channel = [&](int idx) {
+    if (idx < kHeadDim) return kh * kHeadDim + idx;
+    if (idx < 2 * kHeadDim) return a.k_conv + kh * kHeadDim + idx - kHeadDim;
+    return a.v_conv + h * kHeadDim + idx - 2 * kHeadDim;
+  };
+  const int64_t row = b;  // T = 1: token row = sequence
+  float* cs = a.conv_state + row * 3 * a.conv_dim;
+  for (int idx = tid; idx < kStepCh; idx += kRecThreads) {
+    const int c = channel(idx);
+    cp_async16(&s_w[idx], a.conv_w + static_cast<int64_t>(c) * 4);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) cp_async4(&s_hist[i][idx], cs + static_cast<int64_t>(i) * a.conv_dim + c);
+  }
+  float* S = a.state + (static_cast<int64_t>(b) * a.Hv + h) * kHeadDim * kHeadDim;
+  float4 st[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    st[i] = __ldcs(reinterpret_cast<const float4*>(S + (r0 + i) * kHeadDim + c0));
+  griddep_wait();  // the in_proj outputs are ready
+
+  // ---- raw inputs of this thread's channels (tid, and tid + 256 for tid < 128), z, gates: issued while
+  //      the state and history loads are still in flight
+  auto raw = [&](int idx) {
+    if (idx < kHeadDim) return a.q[row * a.q_tok + kh * a.q_head + idx];
+    if (idx < 2 * kHeadDim) return a.k[row * a.k_tok + kh * a.k_head + idx - kHeadDim];
+    return a.v[row * a.v_tok + h * a.v_head + idx - 2 * kHeadDim];
+  };
+  const float x0 = raw(tid);
+  const float x1 = tid < kStepCh - kRecThreads ? raw(tid + kRecThreads) : 0.f;
+  if (tid >= kHeadDim) {  // threads 128..255 have one conv channel, 0..127 two
+    s_z[tid - kHeadDim] = a.z[row * a.z_tok + h * a.z_head + tid - kHeadDim];
+    if (tid == kHeadDim) {
+      s_scal[0] = expf(a.g[row * a.g_tok + h * a.g_head]);
+      s_scal[1] = a.beta[row * a.b_tok + h * a.b_head];
+    }
+  }
+  cp_async_wait_all();              // each thread reads back only the history it copied
+  if (ratio > 1) cluster_arrive();  // this CTA has read the shared q/k history
+
+  // ---- conv + SiLU; the v state (own) rolls now, the q/k state (rank 0) at the end, after the whole
+  //      cluster has read the old history
+  auto conv = [&](int idx, float x) {
+    const float4 w = s_w[idx];
+    const float y = silu_fast(w.x * s_hist[0][idx] + w.y * s_hist[1][idx] + w.z * s_hist[2][idx] + w.w * x);
+    if (idx < kHeadDim) s_q[idx] = y;
+    else if (idx < 2 * kHeadDim) s_k[idx - kHeadDim] = y;
+    else s_v[idx - 2 * kHeadDim] = y;
+  };
+  auto roll = [&](int idx, float x) {
+    const int c = channel(idx);
+    cs[c] = s_hist[1][idx];
+    cs[a.conv_dim + c] = s_hist[2][idx];
+    cs[2 * static_cast<int64_t>(a.conv_dim) + c] = x;
+  };
+  conv(tid, x0);
+  if (tid < kStepCh - kRecThreads) {
+    conv(tid + kRecThreads, x1);
+    roll(tid + kRecThreads, x1);  // v channels 128..255 of this head
+  }
+  __syncthreads();
+  // ---- |q|^2, |k|^2, q.k (warps 0..3)
+  if (tid < kHeadDim) {
+    const float qv = s_q[tid], kv = s_k[tid];
+    float sq = qv * qv, sk = kv * kv, sqk = qv * kv;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      sq += __shfl_xor_sync(0xffffffffu, sq, off);
+      sk += __shfl_xor_sync(0xffffffffu, sk, off);
+      sqk += __shfl_xor_sync(0xffffffffu, sqk, off);
+    }
+    if (lane == 0) {
+      s_red[warp][0] = sq;
+      s_red[warp][1] = sk;
+      s_red[warp][2] = sqk;
+    }
+  }
+  __syncthreads();
+  const float sq = s_red[0][0] + s_red[1][0] + s_red[2][0] + s_red[3][0];
+  const float sk = s_red[0][1] + s_red[1][1] + s_red[2][1] + s_red[3][1];
+  const float sqk = s_red[0][2] + s_red[1][2] + s_red[2][2] + s_red[3][2];
+  const float rq = rsqrtf(sq + 1e-6f) * a.scale, rk = rsqrtf(sk + 1e-6f);
+  const float qk = sqk * rq * rk;
+  const float d = s_scal[0], beta = s_scal[1];
+
+  // ---- decay and the two projections over this thread's 16 rows
+  float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float kr = s_k[r0 + i] * rk, qr = s_q[r0 + i] * rq;
+    float4& s = st[i];
+    s.x *= d;
+    s.y *= d;
+    s.z *= d;
+    s.w *= d;
+    pk.x += kr * s.x; pk.y += kr * s.y; pk.z += kr * s.z; pk.w += kr * s.w;
+    pq.x += qr * s.x; pq.y += qr * s.y; pq.z += qr * s.z; pq.w += qr * s.w;
+  }
+  s_rk[warp][lane] = pk;
+  s_rq[warp][lane] = pq;
+  __syncthreads();
+  if (tid < kHeadDim) {
+    const int quad = tid >> 2, comp = tid & 3;
+    float ks = 0.f, qs = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      ks += reinterpret_cast<const float*>(&s_rk[w][quad])[comp];
+      qs += reinterpret_cast<const float*>(&s_rq[w][quad])[comp];
+    }
+    const float u = beta * (s_v[tid] - ks);
+    const float o = qs + qk * u;
+    s_u[tid] = u;
+    s_o[tid] = o;
+    float so = o * o;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) so += __shfl_xor_sync(0xffffffffu, so, off);
+    if (lane == 0) s_red[warp][3] = so;
+  }
+  __syncthreads();
+  // ---- rank-1 update of the state
+  const float4 u4 = *reinterpret_cast<const float4*>(&s_u[c0]);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float kr = s_k[r0 + i] * rk;
+    st[i].x += kr * u4.x;
+    st[i].y += kr * u4.y;
+    st[i].z += kr * u4.z;
+    st[i].w += kr * u4.w;
+  }
+  // ---- gated RMSNorm output
+  if (tid < kHeadDim) {
+    const float ms = (s_red[0][3] + s_red[1][3] + s_red[2][3] + s_red[3][3]) * (1.0f / kHeadDim);
+    const float y = s_o[tid] * rsqrtf(ms + a.eps) * a.norm_w[tid] * silu_f(s_z[tid]);
+    static_cast<__nv_bfloat16*>(a.y)[row * a.y_tok + h * a.y_head + tid] = __float2bfloat16_rn(y);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) __stcs(reinterpret_cast<float4*>(S + (r0 + i) * kHeadDim + c0), st[i]);
+  // q and k channels, last: by now every sibling has long read the old history
+  if (ratio > 1) cluster_wait();
+  if (ratio == 1 || cluster_ctarank() == 0) roll(tid, x0);
+}
+
+cudaError_t decode_step_forward(const RecurrenceArgs& a, cudaStream_t stream) {
+  if (a.B <= 0 || a.T != 1 || a.Hk <= 0 || a.Hv <= 0 || a.Hv % a.Hk || a.Hv / a.Hk > 8 || !a.z || !a.y ||
+      !a.conv_w || !a.conv_state || a.conv_dim <= 0 || !a.l2norm)
+    return cudaErrorInvalidValue;
+  const int ratio = a.Hv / a.Hk;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.B * a.Hv));
+  cfg.blockDim = dim3(kRecThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (ratio > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = static_cast<unsigned>(ratio);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, decode_step_kernel, a);
+}
+
 }  // namespace gdn

@@ -46,6 +46,7 @@ def _fake_weights():
 @pytest.mark.parametrize("kw, status", [
     (dict(head_k_dim=64), 3), (dict(head_v_dim=256), 3), (dict(conv_kernel=3), 3), (dict(chunk=32), 3),
     (dict(hidden=100), 1), (dict(num_v_heads=3), 1), (dict(num_k_heads=0), 1), (dict(eps=0.0), 1),
+    (dict(num_k_heads=1, num_v_heads=16), 3),
 ])
 def test_layer_create_rejects_bad_geometry(kw, status):
     w, _keep = _fake_weights()

@@ -115,6 +115,21 @@ def test_config3_9b_prefill_at_test_size():
     check("cfg3 conv", layer.get_conv_state(), c, max_rel=1e-4)
 
 
+@pytest.mark.parametrize("hk, hv", [(4, 16), (8, 8)])
+def test_gqa_ratios_prefill_then_decode(hk, hv):
+    """GQA groups of 4 and 1 v-heads per k-head: the decode step keeps the conv in the in_proj epilogue for
+    ratios other than 1 and 2 and runs it in the per-k-head decode kernel otherwise."""
+    w = O.make_weights(1024, hk, hv, seed=40 + hk)
+    B = 3
+    x = O.make_hidden(B, 70, 1024, seed=41)
+    want, s, c = O.layer_forward(w, x, mode="recurrent")
+    layer = Qwen35GatedDeltaNet(weights=w, batch=B)
+    got = torch.cat([layer(x[:, :67])] + [layer(x[:, t:t + 1]) for t in range(67, 70)], 1)
+    check(f"gqa {hk}/{hv} out", got, want)
+    check("state", layer.get_recurrent_state(), s, max_rel=STATE_TOL)
+    check("conv", layer.get_conv_state(), c, max_rel=1e-4)
+
+
 def test_strong_decay_prefill_then_decode():
     """A_log = log(U(1, 64)) (config 4's gate strength): chunk decay underflow must stay finite."""
     w = O.make_weights(1024, 16, 32, seed=4, a_max=64.0)
