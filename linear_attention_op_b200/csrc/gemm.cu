@@ -483,32 +483,40 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
 // One CTA per SM walks the tiles blockIdx.x, + gridDim.x, ... in grouped raster order.  TMEM holds two
 // 128 x 256 fp32 accumulators (all 512 columns): warp 1 issues the MMAs of the next tile into one while
 // the epilogue warps drain the other, and warp 0 keeps the 4-stage ring full across tile boundaries.
+// Eight epilogue warps (two per TMEM lane quarter, one per 128-column half) stage each 64-byte-wide
+// column chunk of their half in shared memory (64B-swizzled) and write it with one TMA tensor store, so
+// the output leaves as whole lines instead of 16-byte pieces of 128 different rows.
 //
 // kEpiPrefillInProj fuses the causal conv (K = 4) + SiLU of the conv channels into the epilogue.  Its
 // M tiles advance by 125 rows and start 3 rows early, so every output row finds its 3 predecessors in
 // the same tile (tile rows 0..2 are recomputed halo and never stored; 2.4% extra MMA work instead of a
 // separate conv pass over HBM).  A row's predecessors sit in the 3 lanes below it (warp shuffles);
 // lanes 0..2 of lane quarters 1..3 take them from the previous quarter's warp through shared memory.
-// Eight epilogue warps (two per TMEM lane quarter, one per 128-column half) keep enough warps issuing
-// to hide the epilogue behind the next tile's MMAs.  Predecessors before
-// the start of a sequence come from conv_state (9B/kernels/layer_reader.cpp:103-124: the conv window
-// continues the cached history); the raw last 3 inputs of each sequence go to conv_tail, from which
-// conv_state_roll_tail() rolls the state after the kernel.
+// Predecessors before the start of a sequence come from conv_state (9B/kernels/layer_reader.cpp:103-124:
+// the conv window continues the cached history); the raw last 3 inputs of each sequence go to conv_tail,
+// from which conv_state_roll_tail() rolls the state after the kernel.  The conv taps of the tile's 256
+// channels are staged in shared memory once per tile.
 constexpr int kPBN = 256;
 constexpr int kPStages = 4;
 constexpr int kConvHalo = 3;
-using PCfg = GemmCfg<kPBN, kPStages>;
-constexpr int kPEpiWarps = 8;  // two per TMEM lane quarter, each draining one 128-column half of a tile
+constexpr int kPEpiWarps = 8;
 constexpr int kPThreads = 64 + 32 * kPEpiWarps;
-constexpr int kPXchOffset = PCfg::kBarOffset + 256;
-constexpr int kPSmemBytes = kPXchOffset + 2 * 2 * 4 * 48 * 4 + 1024;
+using PCfg = GemmCfg<kPBN, kPStages>;
+// Shared memory after the stage ring: barriers | output staging [2 halves][128 rows][64 B] |
+// conv taps [256] float4 | conv exchange [2 halves][4 quarters][3 rows][16] floats.
+constexpr int kPOutStage = PCfg::kBarOffset + 1024;
+constexpr int kPConvW = kPOutStage + 2 * kBM * 64;
+constexpr int kPXch = kPConvW + kPBN * 16;
+constexpr int kPSmemBytes = kPXch + 2 * 4 * 48 * 4 + 1024;
 static_assert(kPSmemBytes <= 227 * 1024, "persistent GEMM shared memory");
+static_assert(kPOutStage % 1024 == 0, "64B-swizzled staging needs 512-byte alignment");
 
-// Named barriers: id 1 + half over the 4 epilogue warps of one column half (conv exchange), id 3 over
-// all 8 epilogue warps (per-tile vote); 0 is __syncthreads.
+// Named barriers: id 1 + half over the 4 epilogue warps of one column half, id 3 (vote) and id 4 over all
+// 8 epilogue warps; 0 is __syncthreads.
 __device__ __forceinline__ void epi_half_sync(int half) {
   asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
 }
+__device__ __forceinline__ void epi_all_sync() { asm volatile("bar.sync 4, 256;" ::: "memory"); }
 __device__ __forceinline__ bool epi_bar_any(bool pred) {
   uint32_t r;
   asm volatile(
@@ -528,10 +536,20 @@ __device__ __forceinline__ void store_f32x16(float* dst, const float (&v)[16]) {
     reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
-// Conv epilogue of one 16-column chunk (columns n0 .. n0 + 15, all conv channels) for tile row r = 32 q +
-// lane, output row `row` (stored when `store`).  xw: this warp's exchange slot, xp: the previous warp's.
-__device__ __forceinline__ void conv_chunk(const GemmEpiArgs& ep, const float (&v)[16], int q, int half, int lane,
-                                           int row, bool store, int n0, float* xw, const float* xp) {
+// Row `srow` of a 64-byte-wide staging tile with the TMA 64B swizzle (16-byte chunk c of row r at chunk
+// c ^ ((r / 2) % 4)); four 16-byte chunks.
+__device__ __forceinline__ void stage_row64(uint8_t* stage, int srow, const uint4 (&c)[4]) {
+  uint8_t* row = stage + srow * 64;
+  const int sw = (srow >> 1) & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(row + ((i ^ sw) << 4)) = c[i];
+}
+
+// Conv of one 16-column chunk (tile columns c0 .. c0 + 15, all conv channels) in place on v, for tile row
+// r = 32 q + lane, output row `row` (valid when `store`).  Ends with the half's first barrier.
+__device__ __forceinline__ void conv_chunk(const GemmEpiArgs& ep, float (&v)[16], int q, int half, int lane,
+                                           int row, bool store, int n0, const float4* cw, float* xw,
+                                           const float* xp) {
   if (lane >= 32 - kConvHalo) store_f32x16(xw + (lane - (32 - kConvHalo)) * 16, v);
   epi_half_sync(half);
   // h1/h2/h3 = inputs at t - 1, t - 2, t - 3.  Predecessor j of lane l < j is lane 32 - j + l of the
@@ -571,23 +589,19 @@ __device__ __forceinline__ void conv_chunk(const GemmEpiArgs& ep, const float (&
       h3[j] = x.x; h3[j + 1] = x.y; h3[j + 2] = x.z; h3[j + 3] = x.w;
     }
   }
-  if (t >= T - kConvHalo) {
-    float* tl = ep.conv_tail + (static_cast<int64_t>(b) * 3 + (t - T + 3)) * cr + n0;
-    store_f32x16(tl, v);
-  }
-  float y[16];
+  if (t >= T - kConvHalo) store_f32x16(ep.conv_tail + (static_cast<int64_t>(b) * 3 + (t - T + 3)) * cr + n0, v);
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const float4 w = __ldg(reinterpret_cast<const float4*>(ep.conv_w) + n0 + j);
-    y[j] = silu_fast(w.x * h3[j] + w.y * h2[j] + w.z * h1[j] + w.w * v[j]);
+    const float4 w = cw[j];
+    v[j] = silu_fast(w.x * h3[j] + w.y * h2[j] + w.z * h1[j] + w.w * v[j]);
   }
-  store_f32x16(static_cast<float*>(ep.out) + static_cast<int64_t>(row) * ep.ld + n0, y);
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(kPThreads, 1)
-    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, int M, int N, int K, int m_stride,
-                           int m_tiles, int n_tiles, int group_m, const uint8_t* b_tiled, GemmEpiArgs ep) {
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmOut,
+                           int M, int N, int K, int m_stride, int m_tiles, int n_tiles, int group_m,
+                           const uint8_t* b_tiled, GemmEpiArgs ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -597,7 +611,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint64_t* acc_full = empty + kPStages;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  float* xch = reinterpret_cast<float*>(smem + kPXchOffset);  // [2 halves][2 chunk parities][4 quarters][3][16]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int halo = kBM - m_stride;
@@ -622,6 +635,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 2 * kPBN);
@@ -716,9 +730,16 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __syncwarp();
   } else {
     griddep_wait();  // the epilogue writes buffers the previous kernel may still read
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;   // column half [128 half, +128) of each tile
+    constexpr int kOutBytes = EPI == kEpiStoreBF16 ? 2 : 4;
+    constexpr int kChunk = 64 / kOutBytes;  // columns per 64-byte staged row: 16 (fp32) or 32 (bf16)
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;       // column half [128 half, +128) of each tile
     const int r = q * 32 + lane;
+    const int etid = (warp - 2) * 32 + lane;
+    const bool issuer = etid == half * 128;  // one thread per half issues the TMA stores
+    uint8_t* stage = smem + kPOutStage + half * kBM * 64;
+    const float4* cw = reinterpret_cast<const float4*>(smem + kPConvW);
+    float* xs = reinterpret_cast<float*>(smem + kPXch) + half * 4 * 48;
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -729,36 +750,92 @@ __global__ void __launch_bounds__(kPThreads, 1)
       coords(t, mt, nt);
       const int row = mt * m_stride - halo + r;
       const bool store = r >= halo && row < M;
+      if constexpr (EPI == kEpiPrefillInProj) {
+        if (nt * kPBN < ep.conv_rows) {  // conv taps of the tile's channels
+          const int c = nt * kPBN + etid;
+          if (c < ep.conv_rows)
+            reinterpret_cast<float4*>(smem + kPConvW)[etid] = __ldg(reinterpret_cast<const float4*>(ep.conv_w) + c);
+          epi_all_sync();
+        }
+      }
       const uint32_t t_row = tmem + static_cast<uint32_t>(a * kPBN) + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-      for (int c0 = half * (kPBN / 2); c0 < (half + 1) * (kPBN / 2); c0 += 16) {
-        float v[16];
-        tmem_ld16(t_row + c0, v);
+      for (int c0 = half * (kPBN / 2); c0 < (half + 1) * (kPBN / 2); c0 += kChunk) {
+        float v[kChunk];
+        tmem_ld16(t_row + c0, *reinterpret_cast<float(*)[16]>(v));
+        if constexpr (kChunk == 32) tmem_ld16(t_row + c0 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
         const int n0 = nt * kPBN + c0;
+        if (issuer) bulk_wait_read();  // the previous store has read the staging rows
+        bool done = false;
         if constexpr (EPI == kEpiPrefillInProj) {
           if (n0 < ep.conv_rows) {
-            float* xs = xch + (half * 2 + ((c0 >> 4) & 1)) * 4 * 48;
-            conv_chunk(ep, v, q, half, lane, row, store, n0, xs + q * 48, xs + (q > 0 ? q - 1 : 0) * 48);
-            continue;
+            conv_chunk(ep, *reinterpret_cast<float(*)[16]>(v), q, half, lane, row, store, n0, cw + c0, xs + q * 48,
+                       xs + (q > 0 ? q - 1 : 0) * 48);
+            done = true;
           }
-          epilogue16<kEpiStoreF32>(ep, store ? row : M, n0, M, N, v);
-        } else {
-          epilogue16<EPI>(ep, store ? row : M, n0, M, N, v);
+        }
+        if (!done) epi_half_sync(half);
+        if (r >= halo) {
+          uint4 c[4];
+          if constexpr (kOutBytes == 4) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              c[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
+                                __float_as_uint(v[4 * i + 3]));
+          } else {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+              w[i] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+          stage_row64(stage, r - halo, c);
+        }
+        fence_proxy_async_shared();
+        epi_half_sync(half);
+        if (issuer) {
+          tma_store_2d(&tmOut, stage, n0, mt * m_stride);
+          bulk_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
+    if (issuer) bulk_wait_all();  // the stores have left shared memory and completed
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, 2 * kPBN);
 }
 
+// Output tensor map of the persistent GEMM: [rows, cols] with row stride ld elements, boxes of 64 bytes
+// (box_cols elements) x box_rows rows, 64-byte swizzle.
+static cudaError_t make_out_tmap(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int64_t ld, bool bf16,
+                                 int box_cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const int es = bf16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * es) & 15) || rows <= 0 || cols <= 0 || ld < cols ||
+      box_cols * es != 64 || box_rows <= 0 || box_rows > 256)
+    return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t est[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims,
+                  strides, box, est, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 template <int EPI>
-static cudaError_t launch_persistent(const CUtensorMap& ta, const void* b_tiled, int M, int N, int K, int m_stride,
-                                     const GemmEpiArgs& ep, bool pdl, cudaStream_t stream) {
+static cudaError_t launch_persistent(const CUtensorMap& ta, const CUtensorMap& to, const void* b_tiled, int M,
+                                     int N, int K, int m_stride, const GemmEpiArgs& ep, bool pdl,
+                                     cudaStream_t stream) {
   auto kern = gemm_persistent_kernel<EPI>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
   if (e != cudaSuccess) return e;
@@ -782,27 +859,33 @@ static cudaError_t launch_persistent(const CUtensorMap& ta, const void* b_tiled,
     cfg.numAttrs = 1;
   }
   count_launch();
-  return cudaLaunchKernelEx(&cfg, kern, ta, M, N, K, m_stride, m_tiles, n_tiles, group_m,
+  return cudaLaunchKernelEx(&cfg, kern, ta, to, M, N, K, m_stride, m_tiles, n_tiles, group_m,
                             static_cast<const uint8_t*>(b_tiled), ep);
 }
 
 cudaError_t gemm_bf16_persistent(const void* A, int64_t lda, const void* B_tiled, int M, int N, int K, int epi,
                                  const GemmEpiArgs& ep, cudaStream_t stream, bool pdl) {
   if (M <= 0 || N <= 0 || K <= 0 || (K & 7) || !B_tiled || !ep.out) return cudaErrorInvalidValue;
-  CUtensorMap ta;
+  CUtensorMap ta, to;
   std::memset(&ta, 0, sizeof(ta));
+  std::memset(&to, 0, sizeof(to));
   cudaError_t e = make_tmap(&ta, A, M, K, lda, kBM);
   if (e != cudaSuccess) return e;
   switch (epi) {
-    case kEpiStoreF32: return launch_persistent<kEpiStoreF32>(ta, B_tiled, M, N, K, kBM, ep, pdl, stream);
-    case kEpiStoreBF16: return launch_persistent<kEpiStoreBF16>(ta, B_tiled, M, N, K, kBM, ep, pdl, stream);
+    case kEpiStoreF32:
+      if ((e = make_out_tmap(&to, ep.out, M, N, ep.ld, false, 16, kBM)) != cudaSuccess) return e;
+      return launch_persistent<kEpiStoreF32>(ta, to, B_tiled, M, N, K, kBM, ep, pdl, stream);
+    case kEpiStoreBF16:
+      if ((e = make_out_tmap(&to, ep.out, M, N, ep.ld, true, 32, kBM)) != cudaSuccess) return e;
+      return launch_persistent<kEpiStoreBF16>(ta, to, B_tiled, M, N, K, kBM, ep, pdl, stream);
     case kEpiPrefillInProj:
       if (ep.seq_len <= 0 || ep.conv_rows <= 0 || (ep.conv_rows & 15) || ep.conv_rows > N || (ep.ld & 3) ||
           (M % ep.seq_len) || !ep.conv_w || !ep.conv_state || !ep.conv_tail ||
-          (reinterpret_cast<uintptr_t>(ep.out) & 15) || (reinterpret_cast<uintptr_t>(ep.conv_state) & 15) ||
-          (reinterpret_cast<uintptr_t>(ep.conv_tail) & 15) || (reinterpret_cast<uintptr_t>(ep.conv_w) & 15))
+          (reinterpret_cast<uintptr_t>(ep.conv_state) & 15) || (reinterpret_cast<uintptr_t>(ep.conv_tail) & 15) ||
+          (reinterpret_cast<uintptr_t>(ep.conv_w) & 15))
         return cudaErrorInvalidValue;
-      return launch_persistent<kEpiPrefillInProj>(ta, B_tiled, M, N, K, kBM - kConvHalo, ep, pdl, stream);
+      if ((e = make_out_tmap(&to, ep.out, M, N, ep.ld, false, 16, kBM - kConvHalo)) != cudaSuccess) return e;
+      return launch_persistent<kEpiPrefillInProj>(ta, to, B_tiled, M, N, K, kBM - kConvHalo, ep, pdl, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -125,6 +125,21 @@ __device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint3
       : "memory");
 }
 
+// 2D tiled store shared -> global of the tensor map's box at (x, y), tracked by this thread's bulk
+// async-group.  The shared source must not be rewritten before bulk_wait_read() returns.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy (TMA, UMMA).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // L2 cache policies (createpolicy): weights are streamed once, activations are re-read by many CTAs.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
