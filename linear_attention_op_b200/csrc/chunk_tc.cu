@@ -23,6 +23,7 @@
 // Precision: every operand is split into bf16 hi + lo and the products that feed the state use three
 // passes (hi*hi + hi*lo + lo*hi, about 16 mantissa bits); the output-only products use hi*hi.  All tiles are
 // K-major with 128-byte swizzle (64 bf16 per row), the layout the GEMM uses.
+#include <cuda.h>
 #include <cuda_bf16.h>
 
 #include "gemm.cuh"
@@ -40,10 +41,10 @@ constexpr int kThreads = 256;
 // e^(G_C - G), 64 floats each, plus 64 unused).
 constexpr int kTImageBytes = 3 * 8192 + 1024;
 constexpr int kTGateOff = 3 * 8192;
-// Per (sequence, k-head, chunk), independent of the gates: [k^ ; q^] hi (2 atoms of [128][64]), k^ lo
-// (2 atoms of [64][64]) and k^T hi / lo ([128 d][64 t] each).
-constexpr int kKImageBytes = 32768 + 16384 + 16384 + 16384;
-constexpr int kKOffKQ = 0, kKOffKL = 32768, kKOffKTH = 49152, kKOffKTL = 65536;
+// Per (sequence, k-head, chunk), independent of the gates: [k^ ; q^] hi (2 atoms of [128][64]) and k^ lo
+// (2 atoms of [64][64]).  MMA1 reads them K-major (over d); MMA3 reads the same k^ rows MN-major (K = t).
+constexpr int kKImageBytes = 32768 + 16384;
+constexpr int kKOffKQ = 0, kKOffKL = 32768;
 
 // Byte offset of bf16 element (r, k), k < 64, in a K-major tile with 128-byte swizzle (1024-aligned base).
 __device__ __forceinline__ uint32_t sw_off(int r, int k) {
@@ -259,26 +260,6 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
       const int idx = tid + i * kThreads, atom = idx >> 9, e = idx & 511;
       reinterpret_cast<uint4*>(ki + kKOffKL + atom * 8192)[e] = reinterpret_cast<const uint4*>(sm.kq_l + atom * 16384)[e];
     }
-    // k^T [d][t]: thread (d, half of the tokens) gathers its column from the swizzled row tiles
-    const int d = tid >> 1, th = tid & 1, atom = d >> 6, kk = d & 63;
-    uint16_t hv[32], lv[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t off = atom * 16384 + sw_off(32 * th + j, kk);
-      hv[j] = *reinterpret_cast<const uint16_t*>(sm.kq_h + off);
-      lv[j] = *reinterpret_cast<const uint16_t*>(sm.kq_l + off);
-    }
-#pragma unroll
-    for (int c8 = 0; c8 < 4; ++c8) {
-      uint32_t wh[4], wl[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        wh[i] = static_cast<uint32_t>(hv[8 * c8 + 2 * i]) | (static_cast<uint32_t>(hv[8 * c8 + 2 * i + 1]) << 16);
-        wl[i] = static_cast<uint32_t>(lv[8 * c8 + 2 * i]) | (static_cast<uint32_t>(lv[8 * c8 + 2 * i + 1]) << 16);
-      }
-      *reinterpret_cast<uint4*>(ki + kKOffKTH + sw_off(d, 32 * th + 8 * c8)) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-      *reinterpret_cast<uint4*>(ki + kKOffKTL + sw_off(d, 32 * th + 8 * c8)) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-    }
   }
 
   __syncthreads();  // the [K; Q] tiles are free: group 1 works in that space from here on
@@ -399,13 +380,15 @@ struct StateSmem {
   uint8_t st_l[32768];   // S^T lo
   uint8_t kimg[kKImageBytes];  // this chunk's k-head operand image (bulk-copied)
   uint8_t tmat[3 * 8192];      // this chunk's T hi, T lo, A hi (bulk-copied)
-  uint8_t rv_h[16384];   // R^T hi [128 v][64 t], later (e^(G_C - G) Vn)^T hi
-  uint8_t rv_l[16384];
-  uint8_t vn_h[16384];   // Vn^T hi
+  // The next chunk's v rows [64 t][128 v] fp32 (bulk-copied, one 512-byte row per token); from phase R on
+  // R^T hi | lo [128 v][64 t], later (e^(G_C - G) Vn)^T hi | lo.
+  uint8_t rv[32768];
+  uint8_t vn_h[16384];     // Vn^T hi
+  float zrows[kC * kD];    // this chunk's z rows [64 t][128 v] fp32 (bulk-copied)
   float gates[2][4 * kC];  // double-buffered beta | e^G | e^(G_C - G)
   float red[4][kC];
   float rstd[kC];
-  uint64_t bar_kq, bar_kt, bar_t, bar_g[2], bar_mma[3];
+  uint64_t bar_kq, bar_t, bar_v, bar_z, bar_g[2], bar_mma[3];
   uint32_t tmem;
   int abort;
 };
@@ -446,8 +429,32 @@ __device__ __forceinline__ void write_row32(uint8_t* hi_tile, uint8_t* lo_tile, 
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, const uint8_t* kimg, const uint8_t* timg,
-                                                                  int nchunks) {
+// Shared-memory descriptor of an MN-major operand with 128-byte swizzle: 64 elements (128 B) contiguous
+// along MN, consecutive K rows 128 B apart in 8-row groups 1024 B apart (SBO), 64-element MN blocks `lbo`
+// bytes apart (LBO); base 1024-byte aligned.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// D (+)= A * B with A [128 x 64] K-major (one SW128 atom) and B = k^ rows [64 t][128 d] read MN-major
+// (the [t][d] atoms of the K image, `lbo` bytes apart): 4 UMMAs of K = 16 tokens.
+__device__ __forceinline__ void mma_a_kmajor_b_mn(uint32_t d, uint32_t a, uint32_t b, uint32_t lbo, uint32_t idesc,
+                                                  bool accumulate) {
+  const uint64_t da = sdesc_k_sw128(a);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    umma_f16(d, da + 2 * k, sdesc_mn_sw128(b + k * 2048, lbo), idesc, (accumulate || k) ? 1u : 0u);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_state_kernel(const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_z, ChunkArgs p,
+                       const uint8_t* kimg, const uint8_t* timg, int nchunks) {
   extern __shared__ uint8_t smem_raw[];
   StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -459,41 +466,51 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
   const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
   const uint8_t* kimg_h = kimg + (static_cast<int64_t>(b) * p.Hk + kh) * nchunks * kKImageBytes;
   const uint8_t* timg_h = timg + (static_cast<int64_t>(b) * p.Hv + h) * nchunks * kTImageBytes;
+  uint8_t* rv_h = sm.rv;
+  uint8_t* rv_l = sm.rv + 16384;
+  const float* vrows = reinterpret_cast<const float*>(sm.rv);
 
-  // Bulk copies of chunk c's images (issued by thread 0 as soon as the buffers they overwrite are free).
-  // Thread 0 counts the copies it issued per barrier, so that after an error it can wait out the ones
-  // still in flight before the CTA exits.
-  int n_kq = 0, n_kt = 0, n_g[2] = {0, 0};
-  auto load_kq = [&](int c) {  // [k^; q^] hi and k^ lo: needed by MMA1
+  // Bulk copies of chunk c's data, each issued as soon as the buffer it overwrites is free.  Thread 0
+  // counts the copies it armed per barrier, so that after an error it can wait out the ones still in flight
+  // before the CTA exits.
+  int n_kq = 0, n_t = 0, n_v = 0, n_z = 0, n_g[2] = {0, 0};
+  auto load_k_t = [&](int c) {  // thread 0: K image (MMA1, MMA3) and T, A (MMA2, MMA3)
     ++n_kq;
-    mbar_arrive_expect_tx(&sm.bar_kq, kKOffKTH);
-    bulk_load(sm.kimg, kimg_h + static_cast<int64_t>(c) * kKImageBytes, kKOffKTH, &sm.bar_kq);
-  };
-  auto load_kt_t = [&](int c) {  // k^T hi/lo (MMA3) and T, A (MMA2, MMA3)
-    ++n_kt;
-    mbar_arrive_expect_tx(&sm.bar_kt, kKImageBytes - kKOffKTH);
-    bulk_load(sm.kimg + kKOffKTH, kimg_h + static_cast<int64_t>(c) * kKImageBytes + kKOffKTH,
-              kKImageBytes - kKOffKTH, &sm.bar_kt);
+    mbar_arrive_expect_tx(&sm.bar_kq, kKImageBytes);
+    bulk_load(sm.kimg, kimg_h + static_cast<int64_t>(c) * kKImageBytes, kKImageBytes, &sm.bar_kq);
+    ++n_t;
     mbar_arrive_expect_tx(&sm.bar_t, 3 * 8192);
     bulk_load(sm.tmat, timg_h + static_cast<int64_t>(c) * kTImageBytes, 3 * 8192, &sm.bar_t);
   };
-  auto load_gates = [&](int c) {
+  auto load_gates = [&](int c) {  // thread 0
     ++n_g[c & 1];
     mbar_arrive_expect_tx(&sm.bar_g[c & 1], 3 * kC * 4);
     bulk_load(sm.gates[c & 1], timg_h + static_cast<int64_t>(c) * kTImageBytes + kTGateOff, 3 * kC * 4,
               &sm.bar_g[c & 1]);
   };
+  // Thread 0: this head's 128 columns of chunk c's 64 token rows (one TMA box; rows past the last token
+  // read as zeros, rows of the next sequence are masked by the reader).
+  auto load_rows = [&](int c, const CUtensorMap* map, int col, void* dst, uint64_t* bar, int& cnt) {
+    ++cnt;
+    mbar_arrive_expect_tx(bar, kC * kD * 4);
+    tma_load_2d(dst, map, bar, col, b * p.T + c * kC, policy_evict_first());
+  };
+  const int v_col = 2 * kd + h * kD, z_col = static_cast<int>(p.z_off) + h * kD;
 
   if (tid == 0) {
     mbar_init(&sm.bar_kq, 1);
-    mbar_init(&sm.bar_kt, 1);
     mbar_init(&sm.bar_t, 1);
+    mbar_init(&sm.bar_v, 1);
+    mbar_init(&sm.bar_z, 1);
     for (int i = 0; i < 2; ++i) mbar_init(&sm.bar_g[i], 1);
     for (int i = 0; i < 3; ++i) mbar_init(&sm.bar_mma[i], 1);
     fence_mbar_init();
     sm.abort = 0;
-    load_kq(0);
-    load_kt_t(0);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_z);
+    load_k_t(0);
+    load_rows(0, &tm_v, v_col, sm.rv, &sm.bar_v, n_v);
+    load_rows(0, &tm_z, z_col, sm.zrows, &sm.bar_z, n_z);
     load_gates(0);
     if (nchunks > 1) load_gates(1);
   }
@@ -514,8 +531,6 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
-  const float* vbase = p.qkv + 2 * kd + h * kD + v;  // v column of this head
-  const float* zbase = p.proj + p.z_off + h * kD + v;
   const float w_norm = p.norm_w[v];
 
   for (int ch = 0; ch < nchunks; ++ch) {
@@ -537,18 +552,19 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
       mma_atoms(tmem + kColP1, sth, 16384, kl, 8192, 2, idesc_dense(1, 128, 64), true);
       umma_commit(&sm.bar_mma[0]);
     }
-    // V for phase R, in flight during MMA1
+    __syncwarp();
+    // V of phase R from the prefetched rows (then the buffer becomes R^T)
+    if (!mbar_wait(&sm.bar_v, par, kErrWaitTmaFull)) sm.abort = 1;
     float vt[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int t = 32 * half + j;
-      vt[j] = t < L ? vbase[(row0 + t) * p.qkv_ld] : 0.f;
+      vt[j] = t < L ? vrows[t * kD + v] : 0.f;
     }
-    __syncwarp();
     if (!mbar_wait(&sm.bar_g[ch & 1], (ch >> 1) & 1, kErrWaitTmaFull)) sm.abort = 1;
     if (!mbar_wait(&sm.bar_mma[0], par, kErrWaitAccum)) sm.abort = 1;
     tc_fence_after();
-    if (tid == 0 && ch + 1 < nchunks) load_kq(ch + 1);  // MMA1 has consumed [K; Q] and k lo
+    __syncthreads();  // every thread has its V: the rows may be overwritten by R^T
     // ---------------- phase R: R^T[v][t] = beta_t (V[t][v] - e^G_t (K^S)^T[v][t]) ----------------
     {
       float ks[32];
@@ -562,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
         ks[4 * j4 + 2] = bt.z * (vt[4 * j4 + 2] - eg.z * ks[4 * j4 + 2]);
         ks[4 * j4 + 3] = bt.w * (vt[4 * j4 + 3] - eg.w * ks[4 * j4 + 3]);
       }
-      write_row32(sm.rv_h, sm.rv_l, v, 32 * half, ks);
+      write_row32(rv_h, rv_l, v, 32 * half, ks);
     }
     fence_async_smem();
     tc_fence_before();
@@ -573,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
     if (tid == 0) {
       if (!mbar_wait(&sm.bar_t, par, kErrWaitTmaFull)) sm.abort = 1;
       tc_fence_after();
-      const uint32_t rh = smem_u32(sm.rv_h), rl = smem_u32(sm.rv_l), th = smem_u32(sm.tmat), tl = smem_u32(sm.tmat + 8192);
+      const uint32_t rh = smem_u32(rv_h), rl = smem_u32(rv_l), th = smem_u32(sm.tmat), tl = smem_u32(sm.tmat + 8192);
       constexpr uint32_t id = idesc_dense(1, 128, 64);
       mma_atoms(tmem + kColVn, rh, 0, th, 0, 1, id, false);
       mma_atoms(tmem + kColVn, rl, 0, th, 0, 1, id, true);
@@ -596,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
         vn[4 * j4 + 2] *= e.z;
         vn[4 * j4 + 3] *= e.w;
       }
-      write_row32(sm.rv_h, sm.rv_l, v, 32 * half, vn);
+      write_row32(rv_h, rv_l, v, 32 * half, vn);
     }
     fence_async_smem();
     tc_fence_before();
@@ -605,28 +621,30 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
     if (sm.abort) break;
     // ---------------- MMA3: dS^T = (e^(G_C-G) Vn)^T K^ ; (A Vn)^T = Vn^T A^T ----------------
     if (tid == 0) {
-      if (!mbar_wait(&sm.bar_kt, par, kErrWaitTmaFull)) sm.abort = 1;
-      tc_fence_after();
-      const uint32_t rh = smem_u32(sm.rv_h), rl = smem_u32(sm.rv_l);
-      const uint32_t kth = smem_u32(sm.kimg + kKOffKTH), ktl = smem_u32(sm.kimg + kKOffKTL);
-      constexpr uint32_t id128 = idesc_dense(1, 128, 128), id64 = idesc_dense(1, 128, 64);
-      mma_atoms(tmem + kColDs, rh, 0, kth, 0, 1, id128, false);
-      mma_atoms(tmem + kColDs, rl, 0, kth, 0, 1, id128, true);
-      mma_atoms(tmem + kColDs, rh, 0, ktl, 0, 1, id128, true);
+      const uint32_t rh = smem_u32(rv_h), rl = smem_u32(rv_l);
+      const uint32_t kq = smem_u32(sm.kimg + kKOffKQ), kl = smem_u32(sm.kimg + kKOffKL);
+      constexpr uint32_t id_mn = idesc_dense(1, 128, 128) | (1u << 16);  // B MN-major
+      constexpr uint32_t id64 = idesc_dense(1, 128, 64);
+      mma_a_kmajor_b_mn(tmem + kColDs, rh, kq, 16384, id_mn, false);
+      mma_a_kmajor_b_mn(tmem + kColDs, rl, kq, 16384, id_mn, true);
+      mma_a_kmajor_b_mn(tmem + kColDs, rh, kl, 8192, id_mn, true);
       mma_atoms(tmem + kColAv, smem_u32(sm.vn_h), 0, smem_u32(sm.tmat + 16384), 0, 1, id64, false);
       umma_commit(&sm.bar_mma[2]);
     }
-    // z for the output, in flight during MMA3
+    __syncwarp();
+    if (!mbar_wait(&sm.bar_z, par, kErrWaitTmaFull)) sm.abort = 1;
     float zt[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = 32 * half + j;
-      zt[j] = t < L ? zbase[(row0 + t) * p.proj_ld] : 0.f;
-    }
-    __syncwarp();
+    for (int j = 0; j < 32; ++j) zt[j] = sm.zrows[(32 * half + j) * kD + v];
     if (!mbar_wait(&sm.bar_mma[2], par, kErrWaitAccum)) sm.abort = 1;
     tc_fence_after();
-    if (tid == 0 && ch + 1 < nchunks) load_kt_t(ch + 1);  // k^T, T and A have been consumed
+    // K image, T, A and the R buffer have been consumed: the next chunk's copies start now
+    if (ch + 1 < nchunks) {  // (also after an error: the exit waits for every armed copy)
+      if (tid == 0) {
+        load_k_t(ch + 1);
+        load_rows(ch + 1, &tm_v, v_col, sm.rv, &sm.bar_v, n_v);
+      }
+    }
     // ---------------- output: O^T[v][t] = e^G_t (Q^S)^T + (A Vn)^T -> RMSNorm over v -> y ----------------
     float o[32];
     {
@@ -666,9 +684,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
       for (int c32 = 0; c32 < 2; ++c32)
         write_row32(sm.st_h + half * 16384, sm.st_l + half * 16384, v, 32 * c32, S + 32 * c32);
     }
-    __syncthreads();  // red[] complete
+    __syncthreads();  // red[] complete; every thread has its z
     if (tid < kC)
       sm.rstd[tid] = rsqrtf((sm.red[0][tid] + sm.red[1][tid] + sm.red[2][tid] + sm.red[3][tid]) * (1.0f / kD) + p.eps);
+    if (tid == 0 && ch + 1 < nchunks) load_rows(ch + 1, &tm_z, z_col, sm.zrows, &sm.bar_z, n_z);
     __syncthreads();
     {
       __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(p.y) + static_cast<int64_t>(h) * kD + v;
@@ -698,10 +717,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_state_kernel(ChunkArgs p, c
   // barrier has parity k & 1; waiting on an already completed phase returns at once.
   if (tid == 0 && sm.abort) {
     if (n_kq) mbar_wait(&sm.bar_kq, (n_kq - 1) & 1, kErrWaitTmaFull);
-    if (n_kt) {
-      mbar_wait(&sm.bar_kt, (n_kt - 1) & 1, kErrWaitTmaFull);
-      mbar_wait(&sm.bar_t, (n_kt - 1) & 1, kErrWaitTmaFull);
-    }
+    if (n_t) mbar_wait(&sm.bar_t, (n_t - 1) & 1, kErrWaitTmaFull);
+    if (n_v) mbar_wait(&sm.bar_v, (n_v - 1) & 1, kErrWaitTmaFull);
+    if (n_z) mbar_wait(&sm.bar_z, (n_z - 1) & 1, kErrWaitTmaFull);
     for (int i = 0; i < 2; ++i)
       if (n_g[i]) mbar_wait(&sm.bar_g[i], (n_g[i] - 1) & 1, kErrWaitTmaFull);
   }
@@ -719,7 +737,9 @@ size_t chunk_prefill_scratch_bytes(int B, int T, int Hk, int Hv) {
 
 static cudaError_t check_chunk_args(const ChunkArgs& a, const void* scratch) {
   if (a.B <= 0 || a.T <= 0 || a.Hk <= 0 || a.Hv <= 0 || a.Hv % a.Hk) return cudaErrorInvalidValue;
-  if ((a.qkv_ld & 3) || (reinterpret_cast<uintptr_t>(scratch) & 15)) return cudaErrorInvalidValue;
+  if ((a.qkv_ld & 3) || (a.proj_ld & 3) || (a.z_off & 3) || (reinterpret_cast<uintptr_t>(scratch) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.qkv) & 15) || (reinterpret_cast<uintptr_t>(a.proj) & 15))
+    return cudaErrorInvalidValue;
   return cudaSuccess;
 }
 
@@ -753,8 +773,15 @@ cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t st
   if (e != cudaSuccess) return e;
   uint8_t *kimg, *timg;
   split_scratch(a, scratch, &kimg, &timg);
+  CUtensorMap tm_v, tm_z;
+  const int64_t n = static_cast<int64_t>(a.B) * a.T;
+  const int kd = a.Hk * kD;
+  e = make_tmap_f32(&tm_v, a.qkv, n, 2 * kd + static_cast<int64_t>(a.Hv) * kD, a.qkv_ld, kD, kC);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_f32(&tm_z, a.proj, n, a.z_off + static_cast<int64_t>(a.Hv) * kD, a.proj_ld, kD, kC);
+  if (e != cudaSuccess) return e;
   count_launch();
-  chunk_state_kernel<<<a.B * a.Hv, kThreads, smem, stream>>>(a, kimg, timg, nchunks);
+  chunk_state_kernel<<<a.B * a.Hv, kThreads, smem, stream>>>(tm_v, tm_z, a, kimg, timg, nchunks);
   return cudaGetLastError();
 }
 
