@@ -55,6 +55,7 @@ struct NcclApi {
   ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*getErrorString)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -71,16 +72,88 @@ static const NcclApi& nccl() {
     api.commInitRank = reinterpret_cast<decltype(api.commInitRank)>(dlsym(h, "ncclCommInitRank"));
     api.commDestroy = reinterpret_cast<decltype(api.commDestroy)>(dlsym(h, "ncclCommDestroy"));
     api.allReduce = reinterpret_cast<decltype(api.allReduce)>(dlsym(h, "ncclAllReduce"));
+    api.allGather = reinterpret_cast<decltype(api.allGather)>(dlsym(h, "ncclAllGather"));
     api.getErrorString = reinterpret_cast<decltype(api.getErrorString)>(dlsym(h, "ncclGetErrorString"));
-    api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.allReduce && api.getErrorString;
+    api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.allReduce && api.allGather &&
+             api.getErrorString;
   });
   return api;
 }
 
+// The communicator: NCCL for prefill, and for decode outputs up to kP2PSlotBytes a one-shot NVLink
+// all-reduce over buffers that every rank maps from every other rank with CUDA IPC.
+// Mapped layout: flags (arrive[8], reduced[8] u64) | epoch u64 | cta_done u32[2] | ... | slot 0 at +4096 |
+// slot 1.
+constexpr size_t kP2PSlotBytes = size_t(8) << 20;
+constexpr size_t kP2PSlotOffset = 4096;
 struct gdn_comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  bool p2p = false;
+  char* sym = nullptr;                       // this rank's mapped page (cudaMalloc)
+  char* peer[kP2PMaxRanks] = {};             // every rank's page in this process (own = sym)
 };
+
+// Maps every rank's page into every process (collective over the NCCL communicator).  On any failure the
+// communicator keeps NCCL only.
+static void p2p_setup(gdn_comm* c) {
+  const NcclApi& api = nccl();
+  if (c->world < 2 || c->world > kP2PMaxRanks) return;
+  // The scratch for the two collectives below comes first: once it exists every rank takes part in both,
+  // even after a local failure (a rank that failed contributes a zero handle and votes no), so no rank
+  // waits for good.
+  cudaStream_t s = nullptr;
+  char* hbuf = nullptr;
+  const size_t hbytes = sizeof(cudaIpcMemHandle_t) * (c->world + 1);
+  if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&hbuf, hbytes + 16) != cudaSuccess) {
+    if (s) cudaStreamDestroy(s);
+    cudaGetLastError();
+    return;
+  }
+  int* flag = reinterpret_cast<int*>(hbuf + hbytes);
+  bool ok = cudaMalloc(&c->sym, kP2PSlotOffset + 2 * kP2PSlotBytes) == cudaSuccess &&
+            cudaMemset(c->sym, 0, kP2PSlotOffset) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  cudaIpcMemHandle_t mine;
+  ok = ok && cudaIpcGetMemHandle(&mine, c->sym) == cudaSuccess;
+  if (!ok) memset(&mine, 0, sizeof(mine));
+  cudaMemcpy(hbuf + sizeof(cudaIpcMemHandle_t) * c->world, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  cudaIpcMemHandle_t all[kP2PMaxRanks];
+  const bool gathered =
+      api.allGather(hbuf + sizeof(cudaIpcMemHandle_t) * c->world, hbuf, sizeof(cudaIpcMemHandle_t), ncclChar, c->comm,
+                    s) == ncclSuccess &&
+      cudaStreamSynchronize(s) == cudaSuccess &&
+      cudaMemcpy(all, hbuf, sizeof(cudaIpcMemHandle_t) * c->world, cudaMemcpyDeviceToHost) == cudaSuccess;
+  ok = ok && gathered;
+  const cudaIpcMemHandle_t zero{};
+  for (int p = 0; ok && p < c->world; ++p) ok = memcmp(&all[p], &zero, sizeof(zero)) != 0;
+  for (int p = 0; ok && p < c->world; ++p) {
+    if (p == c->rank) {
+      c->peer[p] = c->sym;
+      continue;
+    }
+    void* ptr = nullptr;
+    ok = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    c->peer[p] = static_cast<char*>(ptr);
+  }
+  // Agree on the outcome: a rank that failed must not leave the others on the P2P path.
+  int vote = ok ? 1 : 0;
+  cudaMemcpy(flag, &vote, sizeof(int), cudaMemcpyHostToDevice);
+  if (api.allReduce(flag, flag, 1, ncclInt32, ncclMin, c->comm, s) == ncclSuccess &&
+      cudaStreamSynchronize(s) == cudaSuccess && cudaMemcpy(&vote, flag, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess)
+    c->p2p = vote == 1;
+  cudaFree(hbuf);
+  cudaStreamDestroy(s);
+  cudaGetLastError();
+}
+
+static void p2p_teardown(gdn_comm* c) {
+  cudaDeviceSynchronize();
+  for (int p = 0; p < kP2PMaxRanks; ++p)
+    if (c->peer[p] && c->peer[p] != c->sym) cudaIpcCloseMemHandle(c->peer[p]);
+  if (c->sym) cudaFree(c->sym);
+  cudaGetLastError();
+}
 
 // ------------------------------------------------------------------------------------------------
 // Layer
@@ -296,7 +369,8 @@ extern "C" gdn_status gdn_layer_set_stage_events(gdn_layer* L, void* const* even
 // and the conv history while the GEMM runs) -> out_proj, chained by programmatic dependent launch.
 // proj [B, proj_ld] fp32 and y [B, vd] bf16 are scratch.
 static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* rec_state, float* conv_state,
-                               float* proj, __nv_bfloat16* y, uint16_t* out, cudaStream_t stream, bool marks) {
+                               float* proj, __nv_bfloat16* y, uint16_t* out, cudaStream_t stream, bool marks,
+                               const unsigned long long* slot_epoch = nullptr, int64_t slot_bytes = 0) {
   const int h = L->dims.hidden;
   const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
   GemmEpiArgs ep;
@@ -339,6 +413,8 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   eo.out = out;
   eo.ld = h;
   eo.a_tiled = L->w_out;
+  eo.slot_epoch = slot_epoch;
+  eo.slot_bytes = slot_bytes;
   GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
   if (marks) GDN_CUDA(stage_mark(L, 5, stream));
   return GDN_OK;
@@ -369,9 +445,20 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   void* chunk_scratch = ws + lay.chunk;
   const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
 
+  // Tensor parallel: decode outputs are reduced by the NVLink all-reduce, so out_proj writes this rank's
+  // partial into the communicator's mapped slot for this call; prefill outputs by NCCL in place.
+  const int64_t out_elems = n * h;
+  const bool p2p = T == 1 && L->tp_size > 1 && comm && comm->p2p && out_elems % 8 == 0 &&
+                   static_cast<size_t>(out_elems) * 2 <= kP2PSlotBytes;
+  unsigned long long* p2p_epoch = comm ? reinterpret_cast<unsigned long long*>(comm->sym) + 2 * kP2PMaxRanks : nullptr;
+
   GDN_CUDA(stage_mark(L, 0, stream));
   if (T == 1) {
-    gdn_status ds = decode_chain(L, x, B, rec_state, conv_state, proj, y, out, stream, true);
+    gdn_status ds =
+        p2p ? decode_chain(L, x, B, rec_state, conv_state, proj, y,
+                           reinterpret_cast<uint16_t*>(comm->sym + kP2PSlotOffset), stream, true, p2p_epoch,
+                           static_cast<int64_t>(kP2PSlotBytes))
+            : decode_chain(L, x, B, rec_state, conv_state, proj, y, out, stream, true);
     if (ds != GDN_OK) return ds;
   } else {
     // ---- prefill: in_proj with the causal conv + SiLU fused into its epilogue -> conv-state roll ->
@@ -406,7 +493,21 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     GDN_CUDA(gemm_bf16_persistent(y, L->vd, L->w_out, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, stream, true));
     GDN_CUDA(stage_mark(L, 5, stream));
   }
-  if (L->tp_size > 1 && comm) {
+  if (p2p) {
+    P2PAllReduceArgs ar;
+    for (int p = 0; p < comm->world; ++p) {
+      ar.src[p] = comm->peer[p] + kP2PSlotOffset;
+      ar.flags[p] = reinterpret_cast<unsigned long long*>(comm->peer[p]);
+    }
+    ar.epoch = p2p_epoch;
+    ar.cta_done = reinterpret_cast<unsigned int*>(ar.epoch + 1);
+    ar.out = out;
+    ar.n = out_elems;
+    ar.slot_bytes = static_cast<int64_t>(kP2PSlotBytes);
+    ar.rank = comm->rank;
+    ar.world = comm->world;
+    GDN_CUDA(allreduce_p2p(ar, stream));
+  } else if (L->tp_size > 1 && comm) {
     const NcclApi& api = nccl();
     if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
     ncclResult_t r = api.allReduce(out, out, static_cast<size_t>(n) * h, ncclBfloat16, ncclSum, comm->comm, stream);
@@ -549,6 +650,7 @@ extern "C" gdn_status gdn_comm_create(const void* id, size_t id_bytes, int32_t r
   }
   c->rank = rank;
   c->world = world;
+  p2p_setup(c);
   *out = c;
   return GDN_OK;
 }
@@ -556,6 +658,7 @@ extern "C" gdn_status gdn_comm_create(const void* id, size_t id_bytes, int32_t r
 extern "C" gdn_status gdn_comm_destroy(gdn_comm* c) {
   if (!c) return fail(GDN_ERR_NULL_POINTER, "gdn_comm_destroy: null communicator");
   const NcclApi& api = nccl();
+  p2p_teardown(c);
   if (api.ok && c->comm) api.commDestroy(c->comm);
   delete c;
   return GDN_OK;

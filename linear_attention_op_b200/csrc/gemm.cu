@@ -235,8 +235,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int r = q * 32 + lane;     // row inside the tile
   const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
   const bool epi_warp = warp >= 2;
+  GemmEpiArgs eo = ep;
   if (epi_warp) {
     griddep_wait();  // the epilogue writes buffers the previous kernel may still read
+    if (ep.slot_epoch)
+      eo.out = static_cast<char*>(ep.out) + static_cast<int64_t>((*ep.slot_epoch + 1) & 1) * ep.slot_bytes;
     mbar_wait(accum, 0, kErrWaitAccum);
     tc_fence_after();
   }
@@ -247,7 +250,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(t_row + c0, v);
-        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
+        epilogue16<EPI>(eo, m, n_tile * BN + c0, M, N, v);
       }
     }
   } else {
@@ -291,7 +294,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        epilogue16<EPI>(ep, m, n_tile * BN + c0, M, N, v);
+        epilogue16<EPI>(eo, m, n_tile * BN + c0, M, N, v);
       }
     }
     __syncwarp();
@@ -445,6 +448,10 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   else if (N <= 128) BN = 128;
   else BN = 256;
   if (ep.b_tiled && BN < 128) BN = 128;  // a tiled B operand comes in whole 128-row blocks
+  // Weight-streaming (decode) GEMMs keep N tiles of at most 64 tokens: wider batches become more N tiles
+  // that read the same weight blocks at about the same time (one HBM read, the rest L2 hits), instead of
+  // fewer, split-K CTAs.
+  if (ep.a_tiled && BN > 64) BN = 64;
   if ((ep.a_tiled && A != ep.a_tiled) || (ep.b_tiled && B != ep.b_tiled)) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
   std::memset(&ta, 0, sizeof(ta));
@@ -452,17 +459,17 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   cudaError_t e = cudaSuccess;
   if (!ep.a_tiled && (e = make_tmap(&ta, A, M, K, lda, kBM)) != cudaSuccess) return e;
   if (!ep.b_tiled && (e = make_tmap(&tb, B, N, K, ldb, BN)) != cudaSuccess) return e;
-  // Skinny tiles whose A operand is a pre-tiled weight matrix (the decode projections) stream that matrix
-  // from HBM: one CTA per SM with an 8-stage ring (up to 192 KB in flight per SM), split-K only as far as
-  // the whole launch stays one wave, so no CTA waits for another to finish before it starts streaming.
-  // Other skinny tiles use a 3-stage ring (< 75 KB) so three CTAs share an SM; wide tiles take the SM.
-  if (ep.a_tiled && BN <= 64) {
+  // GEMMs whose A operand is a pre-tiled weight matrix (the decode projections) stream that matrix from
+  // HBM: one CTA per SM with a ~190 KB ring in flight, split-K only as far as the whole launch stays one
+  // wave, so no CTA waits for another to finish before it starts streaming.  Other skinny tiles use a
+  // 3-stage ring (< 75 KB) so three CTAs share an SM; wide tiles take the SM.
+  if (ep.a_tiled) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
     if (ksplit <= 0) ksplit = std::max(1, std::min(8, sms / tiles));
-    switch (BN) {
+    switch (BN) {  // rings of 8 stages, up to 8 x 24 KB
       case 16: return dispatch_epi<16, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
       case 32: return dispatch_epi<32, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
       default: return dispatch_epi<64, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);

@@ -82,4 +82,21 @@ size_t chunk_prefill_scratch_bytes(int B, int T, int Hk, int Hv);
 cudaError_t chunk_prep(const ChunkArgs& a, void* scratch, cudaStream_t stream);
 cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t stream);
 
+// NVLink all-reduce (sum) of bf16 [n] partials: src[p] is rank p's first slot (own included, mapped into this
+// process; the second follows slot_bytes later), flags[p] rank p's flag page: arrive[kP2PMaxRanks] then
+// reduced[kP2PMaxRanks] u64 counters.  epoch and cta_done[2] are this rank's device-side control words;
+// call e = epoch + 1 uses slot e % 2.
+constexpr int kP2PMaxRanks = 8;
+struct P2PAllReduceArgs {
+  const void* src[kP2PMaxRanks] = {};
+  unsigned long long* flags[kP2PMaxRanks] = {};
+  unsigned long long* epoch = nullptr;
+  unsigned int* cta_done = nullptr;
+  void* out = nullptr;
+  int64_t n = 0;  // bf16 elements, a multiple of 8
+  int64_t slot_bytes = 0;
+  int rank = 0, world = 1;
+};
+cudaError_t allreduce_p2p(const P2PAllReduceArgs& a, cudaStream_t stream);
+
 }  // namespace gdn

@@ -25,6 +25,7 @@ enum DeviceError : int {
   kErrWaitSmemEmpty = 0x102,   // TMA producer timed out waiting for a free stage
   kErrWaitAccum = 0x103,       // epilogue timed out waiting for the accumulator
   kErrWaitAccEmpty = 0x104,    // MMA issuer timed out waiting for the epilogue to free an accumulator
+  kErrWaitPeer = 0x105,        // all-reduce timed out waiting for a peer rank's flag
   kErrBadArgs = 0x201,         // kernel saw arguments the host should have rejected
 };
 

@@ -1,5 +1,6 @@
-"""Head-parallel layer over 2 (or 4) GPUs with the library's NCCL communicator: every rank gets the full,
-all-reduced output, and the ranks' states tile the single-GPU state.  Skipped with fewer GPUs."""
+"""Head-parallel layer over 2 (or 4) GPUs with the library's communicator (NVLink all-reduce for small
+outputs, NCCL above 8 MiB): every rank gets the full, all-reduced output, and the ranks' states tile the
+single-GPU state.  Skipped with fewer GPUs."""
 import os
 import socket
 
@@ -43,12 +44,17 @@ def _worker(rank, world, port, q):
         s_loc = layer.get_recurrent_state()
         yd = layer(xd)
         s_loc_d = layer.get_recurrent_state()
+        # an output above the NVLink all-reduce's 8 MiB slot (4104 x 1024 bf16) takes the NCCL path
+        xl = O.make_hidden(1, 4104, 1024, seed=9)
+        yl = Qwen35GatedDeltaNet(weights=w, batch=1, tp_rank=rank, tp_size=world, comm=comm)(xl)
         err = device_error()
         hv = 32 // world
         res = dict(
             out=O.max_abs_rel(y.float(), want), state=O.max_abs_rel(s_loc, s_want[:, rank * hv:(rank + 1) * hv]),
             out_dec=O.max_abs_rel(yd.float(), want_d),
             state_dec=O.max_abs_rel(s_loc_d, s_want_d[:, rank * hv:(rank + 1) * hv]), err=err)
+        if rank == 0:
+            res["out_large"] = O.max_abs_rel(yl.float(), O.layer_forward(w, xl, mode="chunk")[0])
         comm.close()
         dist.destroy_process_group()
         q.put((rank, res))
@@ -58,7 +64,7 @@ def _worker(rank, world, port, q):
         q.put((rank, {"exc": traceback.format_exc()}))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tensor_parallel_layer_nccl(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -80,3 +86,5 @@ def test_tensor_parallel_layer_nccl(world):
         assert r["err"] == 0
         assert r["out"] <= 2e-2 and r["out_dec"] <= 2e-2, r
         assert r["state"] <= 1e-3 and r["state_dec"] <= 1e-3, r
+        if rank == 0:
+            assert r["out_large"] <= 2e-2, r
