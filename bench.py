@@ -110,16 +110,21 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices):
+        # One sampler for the whole job (rank 0, its own GPU): nvidia-smi processes polling several GPUs at
+        # once contend for driver locks and stall the ranks' kernel launches.  indices None: no sampling.
+        self.indices = indices
         self.proc = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gdn_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
+        if self.indices is None:
+            return self
         try:
             self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "20"],
+            ids = ",".join(str(i) for i in self.indices)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={ids}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
             t0 = time.time()  # the sampler is running once its first line is out
             while time.time() - t0 < 10 and self.proc.poll() is None and self.path.stat().st_size == 0:
@@ -259,7 +264,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler([local] if rank == 0 else None) as clk:
         torch.cuda.synchronize()
         start.record(stream)
         with torch.cuda.stream(stream):
@@ -353,7 +358,7 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
     torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler([dev.index] if int(os.environ.get("RANK", 0)) == 0 else None) as clk:
         s.record()
         for _ in range(steps):
             layer_p.forward_into(x, out)
