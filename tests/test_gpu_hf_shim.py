@@ -19,8 +19,20 @@ def _hf_layer():
     cfg = Qwen3_5TextConfig(hidden_size=256, linear_num_key_heads=2, linear_num_value_heads=4,
                             linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4,
                             rms_norm_eps=1e-6, num_hidden_layers=1)
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as hf
+
     torch.manual_seed(3)
     L = Qwen3_5GatedDeltaNet(cfg, layer_idx=0).eval()
+    # HF's own torch path (the one the reference's tests run): with a GPU present transformers picks the
+    # flash-linear-attention kernels (conv, delta rule, gated norm), which do not take CPU tensors.
+    L.causal_conv1d_fn = None
+    L.causal_conv1d_update = hf.torch_causal_conv1d_update
+    L.chunk_gated_delta_rule = hf.torch_chunk_gated_delta_rule
+    L.recurrent_gated_delta_rule = hf.torch_recurrent_gated_delta_rule
+    if not isinstance(L.norm, hf.Qwen3_5RMSNormGated):  # the fused norm is a Triton kernel too
+        norm = hf.Qwen3_5RMSNormGated(L.head_v_dim, eps=cfg.rms_norm_eps)
+        norm.weight.data.copy_(L.norm.weight.data)
+        L.norm = norm
     with torch.no_grad():
         L.norm.weight.uniform_(0.5, 1.5)
         L.dt_bias.uniform_(-1.0, 1.0)
