@@ -23,7 +23,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -106,62 +105,71 @@ def prefill_flops(B: int, T: int, world: int = 1) -> dict:
 # Clocks sampled during the timed region
 # ---------------------------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clocks and clock-event (throttle) reasons sampled through NVML in a background thread while the
+    timed region runs (the fields of nvidia-smi's clocks line; read-only queries).  One sampler for the
+    whole job -- rank 0, its own GPU: external nvidia-smi processes polling several GPUs contend for driver
+    locks and stall the ranks' kernel launches.  indices None: no sampling."""
 
-    def __init__(self, indices):
-        # One sampler for the whole job (rank 0, its own GPU): nvidia-smi processes polling several GPUs at
-        # once contend for driver locks and stall the ranks' kernel launches.  indices None: no sampling.
+    def __init__(self, indices, period_s: float | None = 0.05):
+        # period None: only the samples taken as the region starts and ends (used with several ranks, whose
+        # all-reduces make every rank wait out any stall an in-region query causes on one of them)
         self.indices = indices
-        self.proc = None
-        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gdn_clocks_{os.getpid()}.csv"
+        self.period = period_s
+        self.rows = []
+        self.thread = None
+
+    def _sample(self, nv):
+        for h in self.handles:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((sm, mx, rs))
+            except Exception:
+                pass
 
     def __enter__(self):
         if self.indices is None:
             return self
         try:
-            self.fh = open(self.path, "w")
-            ids = ",".join(str(i) for i in self.indices)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={ids}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=self.fh, stderr=subprocess.DEVNULL)
-            t0 = time.time()  # the sampler is running once its first line is out
-            while time.time() - t0 < 10 and self.proc.poll() is None and self.path.stat().st_size == 0:
-                time.sleep(0.02)
-            self.start_size = self.path.stat().st_size
+            import threading
+
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv = nv
+            self.handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in self.indices]
+            self._sample(nv)
+            self.stop = threading.Event()
+
+            def loop():
+                while self.period is not None and not self.stop.wait(self.period):
+                    self._sample(nv)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
+            self.thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.fh.close()
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            self._sample(self.nv)
 
     def summary(self):
-        if self.proc is None or not self.path.exists():
+        if self.thread is None or not self.rows:
             return None
-        rows = []
-        text = self.path.read_text()
-        lines = text[getattr(self, "start_size", 0):].splitlines() or text.splitlines()[-1:]
-        for line in lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        self.path.unlink(missing_ok=True)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        nv = self.nv
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted({name for _, _, rs in self.rows for name, bit in bits.items() if rs & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": reasons, "samples": len(self.rows), "source": "NVML (nvidia-smi's clocks fields)",
+                "mode": "every 50 ms" if self.period else "region start and end (several ranks)"}
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -264,7 +272,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([local] if rank == 0 else None) as clk:
+    with ClockSampler([local] if rank == 0 else None, 0.05 if world == 1 else None) as clk:
         torch.cuda.synchronize()
         start.record(stream)
         with torch.cuda.stream(stream):
@@ -358,7 +366,7 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
     torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([dev.index] if int(os.environ.get("RANK", 0)) == 0 else None) as clk:
+    with ClockSampler([dev.index] if int(os.environ.get("RANK", 0)) == 0 else None, 0.05 if world == 1 else None) as clk:
         s.record()
         for _ in range(steps):
             layer_p.forward_into(x, out)
