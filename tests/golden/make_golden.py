@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference checkout and Hugging Face transformers 5.5.0 are present:
 
-    python tests/golden/make_golden.py [--reference-dir DIR]
+    python tests/golden/make_golden.py --reference-dir <checkout>/wormhole_n150/qwen3.5_9B
 
 Sources of truth (nothing here is re-implemented; every expected value comes from the reference's code):
 
@@ -29,7 +29,6 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REF = "/root/reference/wormhole_n150/qwen3.5_9B"
 
 
 def load_reference_module(ref_dir: str):
@@ -120,7 +119,8 @@ def layer_case() -> dict:
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-dir", default=DEFAULT_REF)
+    ap.add_argument("--reference-dir", required=True,
+                    help="the reference checkout's wormhole_n150/qwen3.5_9B directory (holds reference.py)")
     args = ap.parse_args(argv)
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = load_reference_module(args.reference_dir)
