@@ -138,7 +138,6 @@ struct PrepSmem {
   uint8_t kq_l[2 * 16384];  // [K; Q] lo
   float m[kC * kLdF];
   float t[kC * kLdF];
-  float x[3 * 256];
   float G[kC], beta[kC], eG[kC], eCG[kC];
   uint64_t bar;
   uint32_t tmem;
@@ -237,14 +236,6 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
   // accumulator and work on different v-heads of the GQA group concurrently.
   const int q4 = warp & 3, grp = warp >> 2, gtid = tid & 127;
   const int r = q4 * 32 + lane;
-  float acc[64];
-#pragma unroll
-  for (int c16 = 0; c16 < 4; ++c16) {
-    float v[16];
-    tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 16 * c16, v);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[16 * c16 + i] = v[i];
-  }
   const int t_row = r & 63;
   const bool is_k = r < 64;
   const int tr = gtid >> 1, th = gtid & 1;  // T image writer: (row, 32-column half)
@@ -265,8 +256,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
   __syncthreads();  // the [K; Q] tiles are free: group 1 works in that space from here on
   float* gm = grp ? reinterpret_cast<float*>(sm.kq_h) : sm.m;          // M, then read-only
   float* gt = grp ? gm + kC * kLdF : sm.t;                             // T
-  float* gx = grp ? gt + kC * kLdF : sm.x;                             // block-inverse temporaries
-  float* gG = grp ? gx + 3 * 256 : sm.G;
+  float* gG = grp ? gt + kC * kLdF : sm.G;
   float* gB = gG + kC;                                                 // beta
   float* gE = gB + kC;                                                 // e^G
   float* gC = gE + kC;                                                 // e^(G_C - G)
@@ -282,12 +272,15 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
     if (q4 == 0)
       chunk_gates(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, h, -expf(p.a_log[h]), p.dt_bias[h], lane, gG, gB,
                   gE, gC);
-    // strictly upper blocks of T are zero
-    for (int idx = gtid; idx < 6 * 256; idx += 128) {
-      const int blk = idx >> 8, e = idx & 255;
-      const int ra = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-      const int cb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-      gt[(ra * 16 + (e >> 4)) * kLdF + cb * 16 + (e & 15)] = 0.f;
+    // this warp's TMEM quarter of the [K; Q] K^T accumulator (re-read per head, so no registers stay
+    // allocated to it through the inverse)
+    float acc[64];
+#pragma unroll
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float v[16];
+      tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 16 * c16, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[16 * c16 + i] = v[i];
     }
     group_sync();
     uint8_t* img = timg + ((static_cast<int64_t>(b) * p.Hv + h) * nchunks + ch) * kTImageBytes;
@@ -317,41 +310,29 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
       }
     }
     group_sync();
-    // ---- T = (I + M)^-1: 16 x 16 diagonal blocks by forward substitution, then off-diagonal blocks.
-    {
-      const int o = q4 * 16, jj = lane & 15;
-      if (lane < 16)
-        for (int i = 0; i < 16; ++i) gt[(o + i) * kLdF + o + jj] = (i == jj) ? 1.f : 0.f;
-      __syncwarp();
-      for (int i = 1; i < 16; ++i) {
-        float a = 0.f;
-        if (lane < 16 && jj < i)
-          for (int mm = jj; mm < i; ++mm) a += gm[(o + i) * kLdF + o + mm] * gt[(o + mm) * kLdF + o + jj];
-        __syncwarp();
-        if (lane < 16 && jj < i) gt[(o + i) * kLdF + o + jj] = -a;
-        __syncwarp();
+    // ---- T = (I + M)^-1 by forward substitution, one column per thread: with M strictly lower triangular,
+    //      (I + M) T = I gives T[i][c] = delta(i, c) - sum_{m < i} M[i][m] T[m][c] (zero above the diagonal).
+    //      Rows of M are read as shared-memory broadcasts; the column stays in registers.
+    if (gtid < kC) {
+      const int c = gtid;
+      float tc[kC];
+#pragma unroll
+      for (int i = 0; i < kC; ++i) {
+        const float* mrow = gm + i * kLdF;
+        float a0 = (i == c) ? 1.f : 0.f, a1 = 0.f;
+#pragma unroll
+        for (int m = 0; m + 1 < i; m += 2) {
+          const float2 mm = *reinterpret_cast<const float2*>(mrow + m);
+          a0 -= mm.x * tc[m];
+          a1 -= mm.y * tc[m + 1];
+        }
+        if (i & 1) a0 -= mrow[i - 1] * tc[i - 1];
+        tc[i] = a0 + a1;
       }
+#pragma unroll
+      for (int i = 0; i < kC; ++i) gt[i * kLdF + c] = tc[i];
     }
     group_sync();
-    for (int d = 1; d < 4; ++d) {
-      const int nb = 4 - d;
-      for (int idx = gtid; idx < nb * 256; idx += 128) {  // X = sum_{c=b}^{a-1} M_ac T_cb
-        const int bb = idx >> 8, e = idx & 255, i = e >> 4, jj = e & 15, aa = bb + d;
-        float a = 0.f;
-        for (int c = bb; c < aa; ++c)
-#pragma unroll 4
-          for (int mm = 0; mm < 16; ++mm) a += gm[(aa * 16 + i) * kLdF + c * 16 + mm] * gt[(c * 16 + mm) * kLdF + bb * 16 + jj];
-        gx[idx] = a;
-      }
-      group_sync();
-      for (int idx = gtid; idx < nb * 256; idx += 128) {  // T_ab = -T_aa X
-        const int bb = idx >> 8, e = idx & 255, i = e >> 4, jj = e & 15, aa = bb + d;
-        float a = 0.f;
-        for (int mm = 0; mm <= i; ++mm) a += gt[(aa * 16 + i) * kLdF + aa * 16 + mm] * gx[bb * 256 + mm * 16 + jj];
-        gt[(aa * 16 + i) * kLdF + bb * 16 + jj] = -a;
-      }
-      group_sync();
-    }
     // ---- T image: hi at +0, lo at +8192; thread (row, 32-column half)
     {
       float tv[32];
