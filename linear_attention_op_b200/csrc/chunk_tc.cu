@@ -92,21 +92,36 @@ __device__ __forceinline__ void mma_atoms(uint32_t d, uint32_t a, uint32_t a_str
   }
 }
 
-// Per-chunk gating scalars for v-head h: G (inclusive cumsum of g), beta, e^G, e^(G_C - G).  Warp-level.
-__device__ __forceinline__ void chunk_gates(const float* proj, int64_t proj_ld, int64_t a_off, int64_t b_off,
-                                            int64_t row0, int L, int h, float neg_a, float dtb, int lane, float* G,
+// Raw gate inputs (a, b columns of the in_proj output) of v-head h for the chunk's tokens lane, lane + 32.
+struct GateRaw {
+  float a[2], b[2];
+};
+__device__ __forceinline__ GateRaw gates_load(const float* proj, int64_t proj_ld, int64_t a_off, int64_t b_off,
+                                              int64_t row0, int L, int h, int lane) {
+  GateRaw r;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = lane + 32 * i;
+    r.a[i] = r.b[i] = 0.f;
+    if (t < L) {
+      const float* pr = proj + (row0 + t) * proj_ld;
+      r.a[i] = pr[a_off + h];
+      r.b[i] = pr[b_off + h];
+    }
+  }
+  return r;
+}
+
+// Per-chunk gating scalars of one v-head from its raw inputs: G (inclusive cumsum of g), beta, e^G,
+// e^(G_C - G).  Warp-level.
+__device__ __forceinline__ void chunk_gates(const GateRaw& raw, int L, float neg_a, float dtb, int lane, float* G,
                                             float* beta, float* eG, float* eCG) {
   float g2[2], b2[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int t = lane + 32 * i;
-    g2[i] = 0.f;
-    b2[i] = 0.f;
-    if (t < L) {
-      const float* pr = proj + (row0 + t) * proj_ld;
-      g2[i] = neg_a * softplus_f(pr[a_off + h] + dtb);
-      b2[i] = sigmoid_f(pr[b_off + h]);
-    }
+    g2[i] = t < L ? neg_a * softplus_f(raw.a[i] + dtb) : 0.f;
+    b2[i] = t < L ? sigmoid_f(raw.b[i]) : 0.f;
   }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -165,6 +180,12 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
     tmem_alloc(&sm.tmem, 64);
     tmem_relinquish();
   }
+  // The first v-head of each warp group (heads kh*ratio + 0 and + 1): its gate inputs are requested now,
+  // so their latency hides behind the q/k loads and the MMA.
+  const int grp0 = warp >> 2;
+  GateRaw gate_raw = {};
+  if ((warp & 3) == 0 && grp0 < ratio)
+    gate_raw = gates_load(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, kh * ratio + grp0, lane);
   // ---- q^ and k^ rows, split into bf16 hi/lo: rows 0..63 = k, rows 64..127 = q (4 tokens per warp in flight)
 #pragma unroll 1
   for (int tb = warp; tb < kC; tb += 32) {
@@ -269,9 +290,10 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
 
   for (int j = grp; j < ratio && ok; j += 2) {
     const int h = kh * ratio + j;
-    if (q4 == 0)
-      chunk_gates(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, h, -expf(p.a_log[h]), p.dt_bias[h], lane, gG, gB,
-                  gE, gC);
+    if (q4 == 0) {
+      if (j != grp) gate_raw = gates_load(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, h, lane);
+      chunk_gates(gate_raw, L, -expf(p.a_log[h]), p.dt_bias[h], lane, gG, gB, gE, gC);
+    }
     // this warp's TMEM quarter of the [K; Q] K^T accumulator (re-read per head, so no registers stay
     // allocated to it through the inverse)
     float acc[64];
