@@ -456,8 +456,9 @@ __device__ __forceinline__ void mma_a_kmajor_b_mn(uint32_t d, uint32_t a, uint32
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    chunk_state_kernel(const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_z, ChunkArgs p,
-                       const uint8_t* kimg, const uint8_t* timg, int nchunks) {
+    chunk_state_kernel(const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_z,
+                       const __grid_constant__ CUtensorMap tm_y, ChunkArgs p, const uint8_t* kimg, const uint8_t* timg,
+                       int nchunks) {
   extern __shared__ uint8_t smem_raw[];
   StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -511,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm.abort = 0;
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_z);
+    tma_prefetch_desc(&tm_y);
     load_k_t(0);
     load_rows(0, &tm_v, v_col, sm.rv, &sm.bar_v, n_v);
     load_rows(0, &tm_z, z_col, sm.zrows, &sm.bar_z, n_z);
@@ -546,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* g_eCG = gt + 2 * kC;
     // ---------------- MMA1: [(K^S)^T | (Q^S)^T] = S^T [K^; Q^]^T ----------------
     if (tid == 0) {
+      bulk_wait_read();  // the previous chunk's y tile has left vn_h (rewritten in phase V, after a barrier)
       if (!mbar_wait(&sm.bar_kq, par, kErrWaitTmaFull)) sm.abort = 1;
       tc_fence_after();
       const uint32_t sth = smem_u32(sm.st_h), stl = smem_u32(sm.st_l), kq = smem_u32(sm.kimg + kKOffKQ);
@@ -692,7 +695,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.rstd[tid] = rsqrtf((sm.red[0][tid] + sm.red[1][tid] + sm.red[2][tid] + sm.red[3][tid]) * (1.0f / kD) + p.eps);
     if (tid == 0 && ch + 1 < nchunks) load_rows(ch + 1, &tm_z, z_col, sm.zrows, &sm.bar_z, n_z);
     __syncthreads();
+    // y = O rstd w SiLU(z): a full chunk is staged as a [64 t][128 v] bf16 tile in vn_h (free since MMA3) and
+    // leaves by one TMA store; a partial last chunk is stored directly (the box would spill into the next
+    // sequence's rows).
     {
+      __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(sm.vn_h) + v;
       __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(p.y) + static_cast<int64_t>(h) * kD + v;
       const int64_t y_ld = static_cast<int64_t>(p.Hv) * kD;
 #pragma unroll
@@ -702,7 +709,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = 4 * j4 + u, t = 32 * half + j;
-          if (t < L) yb[(row0 + t) * y_ld] = __float2bfloat16_rn(o[j] * r4[u] * w_norm * silu_fast(zt[j]));
+          const __nv_bfloat16 yv = __float2bfloat16_rn(o[j] * r4[u] * w_norm * silu_fast(zt[j]));
+          if (L == kC) ys[t * kD] = yv;
+          else if (t < L) yb[(row0 + t) * y_ld] = yv;
         }
       }
     }
@@ -710,7 +719,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid == 0 && ch + 2 < nchunks) load_gates(ch + 2);  // this chunk's gate buffer is free again
+    if (tid == 0) {
+      if (L == kC) {
+        tma_store_2d(&tm_y, sm.vn_h, h * kD, static_cast<int>(row0));
+        bulk_commit();
+      }
+      if (ch + 2 < nchunks) load_gates(ch + 2);  // this chunk's gate buffer is free again
+    }
     if (sm.abort) break;
   }
 #pragma unroll
@@ -718,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // After an error the loop may end with bulk copies still in flight into this CTA's shared memory: wait
   // (bounded) for the last phase of every barrier with an issued copy before the CTA exits.  Phase k of a
   // barrier has parity k & 1; waiting on an already completed phase returns at once.
+  if (tid == 0) bulk_wait_all();  // the last y tiles have left shared memory
   if (tid == 0 && sm.abort) {
     if (n_kq) mbar_wait(&sm.bar_kq, (n_kq - 1) & 1, kErrWaitTmaFull);
     if (n_t) mbar_wait(&sm.bar_t, (n_t - 1) & 1, kErrWaitTmaFull);
@@ -776,15 +792,17 @@ cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t st
   if (e != cudaSuccess) return e;
   uint8_t *kimg, *timg;
   split_scratch(a, scratch, &kimg, &timg);
-  CUtensorMap tm_v, tm_z;
+  CUtensorMap tm_v, tm_z, tm_y;
   const int64_t n = static_cast<int64_t>(a.B) * a.T;
   const int kd = a.Hk * kD;
-  e = make_tmap_f32(&tm_v, a.qkv, n, 2 * kd + static_cast<int64_t>(a.Hv) * kD, a.qkv_ld, kD, kC);
+  e = make_tmap_plain(&tm_v, a.qkv, 4, n, 2 * kd + static_cast<int64_t>(a.Hv) * kD, a.qkv_ld, kD, kC);
   if (e != cudaSuccess) return e;
-  e = make_tmap_f32(&tm_z, a.proj, n, a.z_off + static_cast<int64_t>(a.Hv) * kD, a.proj_ld, kD, kC);
+  e = make_tmap_plain(&tm_z, a.proj, 4, n, a.z_off + static_cast<int64_t>(a.Hv) * kD, a.proj_ld, kD, kC);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_plain(&tm_y, a.y, 2, n, static_cast<int64_t>(a.Hv) * kD, static_cast<int64_t>(a.Hv) * kD, kD, kC);
   if (e != cudaSuccess) return e;
   count_launch();
-  chunk_state_kernel<<<a.B * a.Hv, kThreads, smem, stream>>>(tm_v, tm_z, a, kimg, timg, nchunks);
+  chunk_state_kernel<<<a.B * a.Hv, kThreads, smem, stream>>>(tm_v, tm_z, tm_y, a, kimg, timg, nchunks);
   return cudaGetLastError();
 }
 

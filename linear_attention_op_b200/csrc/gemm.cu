@@ -819,20 +819,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 2 * kPBN);
 }
 
-cudaError_t make_tmap_f32(void* map, const float* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
-                          int box_rows) {
+cudaError_t make_tmap_plain(void* map, const void* ptr, int elem_bytes, int64_t rows, int64_t cols, int64_t ld,
+                            int box_cols, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * 4) & 15) || rows <= 0 || cols <= 0 || ld < cols ||
-      (box_cols * 4) & 15 || box_cols <= 0 || box_cols > 256 || box_rows <= 0 || box_rows > 256)
+  if ((elem_bytes != 2 && elem_bytes != 4) || (reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * elem_bytes) & 15) ||
+      rows <= 0 || cols <= 0 || ld < cols || (box_cols * elem_bytes) & 15 || box_cols <= 0 || box_cols > 256 ||
+      box_rows <= 0 || box_rows > 256)
     return cudaErrorInvalidValue;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t est[2] = {1, 1};
-  CUresult r = fn(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
-                  strides, box, est, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(static_cast<CUtensorMap*>(map),
+                  elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(ptr), dims, strides, box, est, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 

@@ -65,10 +65,11 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
 cudaError_t gemm_bf16_persistent(const void* A, int64_t lda, const void* B_tiled, int M, int N, int K, int epi,
                                  const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false);
 
-// Plain (unswizzled) 2D tensor map over an fp32 matrix [rows, cols] with row stride ld elements and boxes of
-// box_cols x box_rows (box_cols * 4 a multiple of 16 bytes).  Needs <cuda.h> for CUtensorMap.
-cudaError_t make_tmap_f32(void* map, const float* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
-                          int box_rows);
+// Plain (unswizzled) 2D tensor map over a matrix [rows, cols] of elem_bytes-byte elements (4: fp32, 2: bf16)
+// with row stride ld elements and boxes of box_cols x box_rows (box_cols * elem_bytes a multiple of 16).
+// `map` points at a CUtensorMap.
+cudaError_t make_tmap_plain(void* map, const void* ptr, int elem_bytes, int64_t rows, int64_t cols, int64_t ld,
+                            int box_cols, int box_rows);
 
 // Weights kept in the GEMM's streaming layout: [ceil(rows/128), rounded up to even][cols/64] blocks of
 // 16 KB, each block the 128B-swizzled shared-memory image of a 128 x 64 bf16 tile, so that a K-slice of
