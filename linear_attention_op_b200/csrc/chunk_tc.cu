@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Bulk copies of chunk c's data, each issued as soon as the buffer it overwrites is free.  Thread 0
   // counts the copies it armed per barrier, so that after an error it can wait out the ones still in flight
   // before the CTA exits.
-  int n_kq = 0, n_t = 0, n_v = 0, n_z = 0, n_g[2] = {0, 0};
+  int n_kq = 0, n_t = 0, n_v = 0, n_z = 0, n_g[2] = {0, 0}, n_mma[3] = {0, 0, 0};
   auto load_k_t = [&](int c) {  // thread 0: K image (MMA1, MMA3) and T, A (MMA2, MMA3)
     ++n_kq;
     mbar_arrive_expect_tx(&sm.bar_kq, kKImageBytes);
@@ -538,6 +538,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem;
   const float w_norm = p.norm_w[v];
 
+  // MMA1 of chunk c: [(K^S)^T | (Q^S)^T] = S^T [K^; Q^]^T (thread 0)
+  auto issue_mma1 = [&](int c) {
+    if (!mbar_wait(&sm.bar_kq, c & 1, kErrWaitTmaFull)) sm.abort = 1;
+    tc_fence_after();
+    const uint32_t sth = smem_u32(sm.st_h), stl = smem_u32(sm.st_l), kq = smem_u32(sm.kimg + kKOffKQ);
+    const uint32_t kl = smem_u32(sm.kimg + kKOffKL);
+    mma_atoms(tmem + kColP1, sth, 16384, kq, 16384, 2, idesc_dense(1, 128, 128), false);
+    mma_atoms(tmem + kColP1, stl, 16384, kq, 16384, 2, idesc_dense(1, 128, 128), true);
+    mma_atoms(tmem + kColP1, sth, 16384, kl, 8192, 2, idesc_dense(1, 128, 64), true);
+    umma_commit(&sm.bar_mma[0]);
+    ++n_mma[0];
+  };
+
   for (int ch = 0; ch < nchunks; ++ch) {
     const int t0 = ch * kC, L = min(kC, p.T - t0);
     const int64_t row0 = static_cast<int64_t>(b) * p.T + t0;
@@ -546,17 +559,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* g_beta = gt;
     const float* g_eG = gt + kC;
     const float* g_eCG = gt + 2 * kC;
-    // ---------------- MMA1: [(K^S)^T | (Q^S)^T] = S^T [K^; Q^]^T ----------------
     if (tid == 0) {
-      bulk_wait_read();  // the previous chunk's y tile has left vn_h (rewritten in phase V, after a barrier)
-      if (!mbar_wait(&sm.bar_kq, par, kErrWaitTmaFull)) sm.abort = 1;
-      tc_fence_after();
-      const uint32_t sth = smem_u32(sm.st_h), stl = smem_u32(sm.st_l), kq = smem_u32(sm.kimg + kKOffKQ);
-      const uint32_t kl = smem_u32(sm.kimg + kKOffKL);
-      mma_atoms(tmem + kColP1, sth, 16384, kq, 16384, 2, idesc_dense(1, 128, 128), false);
-      mma_atoms(tmem + kColP1, stl, 16384, kq, 16384, 2, idesc_dense(1, 128, 128), true);
-      mma_atoms(tmem + kColP1, sth, 16384, kl, 8192, 2, idesc_dense(1, 128, 64), true);
-      umma_commit(&sm.bar_mma[0]);
+      bulk_wait_read();  // the previous chunk's y tile has left vn_h (rewritten in phase V)
+      issue_mma1(ch);
     }
     __syncwarp();
     // V of phase R from the prefetched rows (then the buffer becomes R^T)
@@ -601,6 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_atoms(tmem + kColVn, rl, 0, th, 0, 1, id, true);
       mma_atoms(tmem + kColVn, rh, 0, tl, 0, 1, id, true);
       umma_commit(&sm.bar_mma[1]);
+      ++n_mma[1];
     }
     __syncwarp();
     if (!mbar_wait(&sm.bar_mma[1], par, kErrWaitAccum)) sm.abort = 1;
@@ -636,6 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_a_kmajor_b_mn(tmem + kColDs, rh, kl, 8192, id_mn, true);
       mma_atoms(tmem + kColAv, smem_u32(sm.vn_h), 0, smem_u32(sm.tmat + 16384), 0, 1, id64, false);
       umma_commit(&sm.bar_mma[2]);
+      ++n_mma[2];
     }
     __syncwarp();
     if (!mbar_wait(&sm.bar_z, par, kErrWaitTmaFull)) sm.abort = 1;
@@ -690,7 +697,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c32 = 0; c32 < 2; ++c32)
         write_row32(sm.st_h + half * 16384, sm.st_l + half * 16384, v, 32 * c32, S + 32 * c32);
     }
-    __syncthreads();  // red[] complete; every thread has its z
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();  // red[] complete; every thread has its z; S^T is written
+    tc_fence_after();
     if (tid < kC)
       sm.rstd[tid] = rsqrtf((sm.red[0][tid] + sm.red[1][tid] + sm.red[2][tid] + sm.red[3][tid]) * (1.0f / kD) + p.eps);
     if (tid == 0 && ch + 1 < nchunks) load_rows(ch + 1, &tm_z, z_col, sm.zrows, &sm.bar_z, n_z);
@@ -730,8 +740,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 #pragma unroll
   for (int j = 0; j < 64; ++j) Sg[(64 * half + j) * kD + v] = S[j];
-  // After an error the loop may end with bulk copies still in flight into this CTA's shared memory: wait
-  // (bounded) for the last phase of every barrier with an issued copy before the CTA exits.  Phase k of a
+  // After an error the loop may end with bulk copies still in flight into this CTA's shared memory, and MMAs
+  // still writing TMEM: wait (bounded) for the last phase of every barrier with an issued copy or commit
+  // before the CTA exits.  Phase k of a
   // barrier has parity k & 1; waiting on an already completed phase returns at once.
   if (tid == 0) bulk_wait_all();  // the last y tiles have left shared memory
   if (tid == 0 && sm.abort) {
@@ -741,6 +752,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (n_z) mbar_wait(&sm.bar_z, (n_z - 1) & 1, kErrWaitTmaFull);
     for (int i = 0; i < 2; ++i)
       if (n_g[i]) mbar_wait(&sm.bar_g[i], (n_g[i] - 1) & 1, kErrWaitTmaFull);
+    // and for the last MMA group committed on each barrier, before TMEM is freed
+    for (int i = 0; i < 3; ++i)
+      if (n_mma[i]) mbar_wait(&sm.bar_mma[i], (n_mma[i] - 1) & 1, kErrWaitAccum);
   }
   tc_fence_before();
   __syncthreads();
