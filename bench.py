@@ -112,11 +112,23 @@ class ClockSampler:
 
     def __init__(self, indices, period_s: float | None = 0.05):
         # period None: only the samples taken as the region starts and ends (used with several ranks, whose
-        # all-reduces make every rank wait out any stall an in-region query causes on one of them)
+        # all-reduces make every rank wait out any stall an in-region query causes on one of them).  NVML is
+        # initialised here, before the caller's barrier: nvmlInit takes long enough that doing it as the
+        # region starts would delay rank 0 behind the others.
         self.indices = indices
         self.period = period_s
         self.rows = []
         self.thread = None
+        self.handles = None
+        if indices is not None:
+            try:
+                import pynvml as nv
+
+                nv.nvmlInit()
+                self.nv = nv
+                self.handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in indices]
+            except Exception:
+                self.handles = None
 
     def _sample(self, nv):
         for h in self.handles:
@@ -129,16 +141,12 @@ class ClockSampler:
                 pass
 
     def __enter__(self):
-        if self.indices is None:
+        if not self.handles:
             return self
         try:
             import threading
 
-            import pynvml as nv
-
-            nv.nvmlInit()
-            self.nv = nv
-            self.handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in self.indices]
+            nv = self.nv
             self._sample(nv)
             self.stop = threading.Event()
 
@@ -270,10 +278,16 @@ def run_ours(args):
     for _ in range(max(1, -(-args.warmup // gsteps))):
         graph.replay()
     torch.cuda.synchronize()
+    sampler = ClockSampler([local] if rank == 0 else None, 0.05 if world == 1 else None)
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([local] if rank == 0 else None, 0.05 if world == 1 else None) as clk:
+    with sampler as clk:
         torch.cuda.synchronize()
+        if world > 1:
+            # One more untimed replay: its all-reduces line the ranks' devices up, so the timed region starts
+            # at the same moment on every rank whatever host-side skew follows the barrier.
+            with torch.cuda.stream(stream):
+                graph.replay()
         start.record(stream)
         with torch.cuda.stream(stream):
             for _ in range(args.steps // gsteps):
@@ -364,9 +378,13 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
     for _ in range(2):
         layer_p.forward_into(x, out)
     torch.cuda.synchronize()
+    sampler = ClockSampler([dev.index] if int(os.environ.get("RANK", 0)) == 0 else None, 0.05 if world == 1 else None)
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([dev.index] if int(os.environ.get("RANK", 0)) == 0 else None, 0.05 if world == 1 else None) as clk:
+    with sampler as clk:
+        torch.cuda.synchronize()
+        if world > 1:  # an untimed step whose all-reduce lines the ranks' devices up (as in decode)
+            layer_p.forward_into(x, out)
         s.record()
         for _ in range(steps):
             layer_p.forward_into(x, out)

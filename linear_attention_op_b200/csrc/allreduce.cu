@@ -8,9 +8,12 @@
 //      (bounded) until every rank's announcement is visible in its own flag page;
 //   2. two ranks: sums both partials in rank order straight from the peers' slots (one shot);
 //      more ranks: reduce-scatter + all-gather -- rank r sums slice r of every partial (rank order) into
-//      slice r of its own slot and of the output, announces "slice reduced" (reduced[rank]) once every CTA
-//      has written its part, waits for every rank's, then copies the other ranks' reduced slices;
+//      slice r of its own slot and of the output; each CTA then announces its share of the slice
+//      (reduced[rank][cta]) and copies the same share of every other rank's reduced slice once that rank's
+//      CTA of the same index has announced it;
 //   3. advances the epoch once every CTA has read it.
+// The kernel lets the next kernel in the stream launch as soon as it starts (programmatic dependent
+// launch): the next step's in_proj streams its weights while this kernel waits on its peers.
 // Every rank computes identical bits (rank-order sums).  No rank rewrites a slot a peer may still read: a
 // rank writes slot e % 2 again only at call e + 2, after its call e + 1 saw every peer arrive at e + 1,
 // which each peer does only after finishing its call e.  The epoch lives in device memory, so the kernel
@@ -63,6 +66,19 @@ __device__ __forceinline__ bool cta_wait_all(const unsigned long long* flags, in
   return *s_abort == 0;
 }
 
+// Thread 0 waits for flags[p * stride] >= e for p in [0, world); the CTA learns the outcome.
+__device__ __forceinline__ bool cta_wait_all_stride(const unsigned long long* flags, int stride, int world,
+                                                    unsigned long long e, int* s_abort) {
+  if (threadIdx.x == 0)
+    for (int p = 0; p < world; ++p)
+      if (!wait_flag(flags + static_cast<int64_t>(p) * stride, e)) {
+        *s_abort = 1;
+        break;
+      }
+  __syncthreads();
+  return *s_abort == 0;
+}
+
 // Sum of the world partials of 8 bf16 (vector i of each slot), in rank order.
 __device__ __forceinline__ uint4 sum8(const P2PAllReduceArgs& a, int64_t slot, int64_t i) {
   uint4 v[kP2PMaxRanks];
@@ -96,6 +112,9 @@ __global__ void __launch_bounds__(256) allreduce_p2p_kernel(P2PAllReduceArgs a) 
   // Launched with programmatic dependent launch: it starts once out_proj has finished and its partial is
   // in memory.
   griddep_wait();
+  // The next kernel (the next step's in_proj) may start streaming its weights now; its own dependent
+  // wait still orders every read of this kernel's output after this grid completes.
+  griddep_launch_dependents();
   const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(a.epoch) + 1;
   if (threadIdx.x == 0) s_abort = 0;
   __syncthreads();
@@ -120,20 +139,24 @@ __global__ void __launch_bounds__(256) allreduce_p2p_kernel(P2PAllReduceArgs a) 
       mine[i] = o;
       out[i] = o;
     }
+    // CTA c of every rank covers the same offsets inside each slice, so CTA c of rank p copies exactly
+    // what CTA c of rank r reduced: a per-CTA "reduced" flag replaces a grid-wide barrier.
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(a.cta_done + 1, 1u) == gridDim.x - 1) {
-      a.cta_done[1] = 0u;
-      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + kP2PMaxRanks + a.rank, e);
-    }
-    // 2b. all-gather of the other ranks' reduced slices
-    ok = cta_wait_all(a.flags[a.rank] + kP2PMaxRanks, a.world, e, &s_abort);
+    if (threadIdx.x < a.world)
+      st_release_sys(a.flags[threadIdx.x] + kP2PReducedOff + a.rank * kP2PMaxCtas + blockIdx.x, e);
+    // 2b. all-gather of the other ranks' reduced slices, every peer's load in flight at once
+    ok = cta_wait_all_stride(a.flags[a.rank] + kP2PReducedOff + blockIdx.x, kP2PMaxCtas, a.world, e, &s_abort);
     if (ok) {
-      for (int p = 0; p < a.world; ++p) {
-        if (p == a.rank) continue;
-        const uint4* theirs = reinterpret_cast<const uint4*>(static_cast<const char*>(a.src[p]) + slot);
-        const int64_t plo = per * p, phi = min(nv, plo + per);
-        for (int64_t i = plo + tid0; i < phi; i += stride) out[i] = __ldcg(theirs + i);
+      for (int64_t k = tid0; k < per; k += stride) {
+        uint4 v[kP2PMaxRanks];
+#pragma unroll
+        for (int p = 0; p < kP2PMaxRanks; ++p)
+          if (p < a.world && p != a.rank && per * p + k < nv)
+            v[p] = __ldcg(reinterpret_cast<const uint4*>(static_cast<const char*>(a.src[p]) + slot) + per * p + k);
+#pragma unroll
+        for (int p = 0; p < kP2PMaxRanks; ++p)
+          if (p < a.world && p != a.rank && per * p + k < nv) out[per * p + k] = v[p];
       }
     }
   }
@@ -155,7 +178,7 @@ cudaError_t allreduce_p2p(const P2PAllReduceArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t nv = a.n / 8;
-  const int grid = static_cast<int>(std::min<int64_t>(sms, (nv + 255) / 256));
+  const int grid = static_cast<int>(std::min<int64_t>(std::min(sms, kP2PMaxCtas), (nv + 255) / 256));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(256);

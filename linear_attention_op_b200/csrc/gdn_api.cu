@@ -82,10 +82,11 @@ static const NcclApi& nccl() {
 
 // The communicator: NCCL for prefill, and for decode outputs up to kP2PSlotBytes a one-shot NVLink
 // all-reduce over buffers that every rank maps from every other rank with CUDA IPC.
-// Mapped layout: flags (arrive[8], reduced[8] u64) | epoch u64 | cta_done u32[2] | ... | slot 0 at +4096 |
-// slot 1.
+// Mapped layout: flag page (arrive[8] u64 | ... | epoch u64 at [16] | cta_done u32[2] at [17] | ... |
+// reduced[rank][cta] u64 from [kP2PReducedOff]) | slot 0 at +kP2PSlotOffset | slot 1.
 constexpr size_t kP2PSlotBytes = size_t(8) << 20;
-constexpr size_t kP2PSlotOffset = 4096;
+constexpr size_t kP2PSlotOffset = 32768;
+static_assert(kP2PFlagPageBytes <= static_cast<int>(kP2PSlotOffset), "flag page overlaps slot 0");
 struct gdn_comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;

@@ -83,10 +83,13 @@ cudaError_t chunk_prep(const ChunkArgs& a, void* scratch, cudaStream_t stream);
 cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t stream);
 
 // NVLink all-reduce (sum) of bf16 [n] partials: src[p] is rank p's first slot (own included, mapped into this
-// process; the second follows slot_bytes later), flags[p] rank p's flag page: arrive[kP2PMaxRanks] then
-// reduced[kP2PMaxRanks] u64 counters.  epoch and cta_done[2] are this rank's device-side control words;
-// call e = epoch + 1 uses slot e % 2.
+// process; the second follows slot_bytes later), flags[p] rank p's flag page: arrive[kP2PMaxRanks] u64
+// counters at [0], reduced[kP2PMaxRanks][kP2PMaxCtas] at [kP2PReducedOff].  epoch and cta_done[2] are this
+// rank's device-side control words; call e = epoch + 1 uses slot e % 2.
 constexpr int kP2PMaxRanks = 8;
+constexpr int kP2PMaxCtas = 256;    // all-reduce grid cap
+constexpr int kP2PReducedOff = 64;  // u64 index of reduced[rank][cta] in a flag page
+constexpr int kP2PFlagPageBytes = (kP2PReducedOff + kP2PMaxRanks * kP2PMaxCtas) * 8;
 struct P2PAllReduceArgs {
   const void* src[kP2PMaxRanks] = {};
   unsigned long long* flags[kP2PMaxRanks] = {};
