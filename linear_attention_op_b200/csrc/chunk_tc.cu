@@ -186,12 +186,13 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
   GateRaw gate_raw = {};
   if ((warp & 3) == 0 && grp0 < ratio)
     gate_raw = gates_load(p.proj, p.proj_ld, p.a_off, p.b_off, row0, L, kh * ratio + grp0, lane);
-  // ---- q^ and k^ rows, split into bf16 hi/lo: rows 0..63 = k, rows 64..127 = q (4 tokens per warp in flight)
-#pragma unroll 1
-  for (int tb = warp; tb < kC; tb += 32) {
-    float4 qv[4], kv[4];
+  // ---- q^ and k^ rows, split into bf16 hi/lo: rows 0..63 = k, rows 64..127 = q (all 8 tokens of a warp in
+  //      flight at once)
+  {
+    const int tb = warp;
+    float4 qv[8], kv[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int t = tb + 8 * u;
       qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       kv[u] = qv[u];
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int t = tb + 8 * u;
       float sq = qv[u].x * qv[u].x + qv[u].y * qv[u].y + qv[u].z * qv[u].z + qv[u].w * qv[u].w;
       float sk = kv[u].x * kv[u].x + kv[u].y * kv[u].y + kv[u].z * kv[u].z + kv[u].w * kv[u].w;
@@ -332,34 +333,106 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
       }
     }
     group_sync();
-    // ---- T = (I + M)^-1 by forward substitution, one column per thread: with M strictly lower triangular,
-    //      (I + M) T = I gives T[i][c] = delta(i, c) - sum_{m < i} M[i][m] T[m][c] (zero above the diagonal).
-    //      Rows of M are read as shared-memory broadcasts; the column stays in registers.
+    // ---- T = (I + M)^-1 with M strictly lower triangular, by 16 x 16 blocks (T_ij = block (i, j)):
+    //   1. diagonal blocks T_bb = (I + M_bb)^-1 by forward substitution, one column per thread:
+    //      T[i][c] = delta(i, c) - sum_{m < i} M[i][m] T[m][c] (exact zeros above the diagonal);
+    //   2. T_10 = -T_11 M_10 T_00 and T_32 = -T_33 M_32 T_22, one column per thread;
+    //   3. the lower-left 32 x 32 quarter: W = M_[23][01] T_[01][01], then T_[23][01] = -T_[23][23] W.
+    //   Blocks (0, 1) and (2, 3) are zeroed for step 3; the other entries above the diagonal are never
+    //   written (the image writer masks them).  W lives in the unused upper-right quarter of M.
     if (gtid < kC) {
-      const int c = gtid;
-      float tc[kC];
+      const int o = 16 * (gtid >> 4), c = gtid & 15;
+      float x[16];
 #pragma unroll
-      for (int i = 0; i < kC; ++i) {
-        const float* mrow = gm + i * kLdF;
+      for (int i = 0; i < 16; ++i) {
+        const float* mrow = gm + (o + i) * kLdF + o;
         float a0 = (i == c) ? 1.f : 0.f, a1 = 0.f;
 #pragma unroll
         for (int m = 0; m + 1 < i; m += 2) {
           const float2 mm = *reinterpret_cast<const float2*>(mrow + m);
-          a0 -= mm.x * tc[m];
-          a1 -= mm.y * tc[m + 1];
+          a0 -= mm.x * x[m];
+          a1 -= mm.y * x[m + 1];
         }
-        if (i & 1) a0 -= mrow[i - 1] * tc[i - 1];
-        tc[i] = a0 + a1;
+        if (i & 1) a0 -= mrow[i - 1] * x[i - 1];
+        x[i] = a0 + a1;
       }
 #pragma unroll
-      for (int i = 0; i < kC; ++i) gt[i * kLdF + c] = tc[i];
+      for (int i = 0; i < 16; ++i) gt[(o + i) * kLdF + o + c] = x[i];
+    } else {
+      const int z = gtid - kC, blk = z >> 5, row = (z & 31) >> 1, half = z & 1;
+      float4* dst = reinterpret_cast<float4*>(gt + (32 * blk + row) * kLdF + 32 * blk + 16 + 8 * half);
+      dst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     group_sync();
-    // ---- T image: hi at +0, lo at +8192; thread (row, 32-column half)
+    if (gtid < 32) {
+      const int o = 32 * (gtid >> 4), c = gtid & 15;
+      float tcol[16], w[16];
+#pragma unroll
+      for (int m = 0; m < 16; ++m) tcol[m] = gt[(o + m) * kLdF + o + c];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {  // w = M_(o+16, o) T_(o, o)[:, c]
+        const float4* mrow = reinterpret_cast<const float4*>(gm + (o + 16 + r) * kLdF + o);
+        float acc = 0.f;
+#pragma unroll
+        for (int m4 = 0; m4 < 4; ++m4) {
+          const float4 mm = mrow[m4];
+          acc += mm.x * tcol[4 * m4] + mm.y * tcol[4 * m4 + 1] + mm.z * tcol[4 * m4 + 2] + mm.w * tcol[4 * m4 + 3];
+        }
+        w[r] = acc;
+      }
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {  // T_(o+16, o)[:, c] = -T_(o+16, o+16) w
+        const float* trow = gt + (o + 16 + r) * kLdF + o + 16;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m <= r; ++m) acc += trow[m] * w[m];
+        gt[(o + 16 + r) * kLdF + o + c] = -acc;
+      }
+    }
+    group_sync();
+    const int c32 = gtid & 31, r8 = 8 * (gtid >> 5);
+    {
+      float tcol[32], acc[8];
+#pragma unroll
+      for (int m = 0; m < 32; ++m) tcol[m] = gt[m * kLdF + c32];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float4* mrow = reinterpret_cast<const float4*>(gm + (32 + r8 + r) * kLdF);
+        float a = 0.f;
+#pragma unroll
+        for (int m4 = 0; m4 < 8; ++m4) {
+          const float4 mm = mrow[m4];
+          a += mm.x * tcol[4 * m4] + mm.y * tcol[4 * m4 + 1] + mm.z * tcol[4 * m4 + 2] + mm.w * tcol[4 * m4 + 3];
+        }
+        acc[r] = a;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) gm[(r8 + r) * kLdF + 32 + c32] = acc[r];
+    }
+    group_sync();
+    {
+      float wcol[32];
+#pragma unroll
+      for (int m = 0; m < 32; ++m) wcol[m] = gm[m * kLdF + 32 + c32];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float4* trow = reinterpret_cast<const float4*>(gt + (32 + r8 + r) * kLdF + 32);
+        float a = 0.f;
+#pragma unroll
+        for (int m4 = 0; m4 < 8; ++m4) {
+          const float4 tt = trow[m4];
+          a += tt.x * wcol[4 * m4] + tt.y * wcol[4 * m4 + 1] + tt.z * wcol[4 * m4 + 2] + tt.w * wcol[4 * m4 + 3];
+        }
+        gt[(32 + r8 + r) * kLdF + c32] = -a;
+      }
+    }
+    group_sync();
+    // ---- T image: hi at +0, lo at +8192; thread (row, 32-column half); entries above the diagonal are 0
     {
       float tv[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) tv[i] = gt[tr * kLdF + 32 * th + i];
+      for (int i = 0; i < 32; ++i) tv[i] = 32 * th + i <= tr ? gt[tr * kLdF + 32 * th + i] : 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
         uint4 hi, lo;

@@ -369,8 +369,7 @@ static int cluster_capacity(Kern kern, int ks, int smem) {
 // Split-K factor that minimises (waves of clusters) x (k-blocks per slice), from the real cluster
 // occupancy; ties go to the smaller split.
 template <class Kern>
-static int choose_ksplit(Kern kern, int smem, int tiles, int kblocks) {
-  static int cap[9] = {0};  // per kernel instantiation, filled on first use
+static int choose_ksplit(Kern kern, int smem, int tiles, int kblocks, int (&cap)[9]) {
   int best = 1;
   double best_cost = 1e30;
   for (int ks = 1; ks <= 8 && ks <= kblocks; ++ks) {
@@ -385,6 +384,17 @@ static int choose_ksplit(Kern kern, int smem, int tiles, int kblocks) {
   return best;
 }
 
+// Weight-streaming GEMMs: the largest split in [1, kmax] whose clusters all fit on the device at once (one
+// wave), else 1.
+template <class Kern>
+static int one_wave_ksplit(Kern kern, int smem, int tiles, int kmax, int (&cap)[9]) {
+  for (int ks = std::min(kmax, 8); ks > 1; --ks) {
+    if (!cap[ks]) cap[ks] = cluster_capacity(kern, ks, smem);
+    if (tiles <= cap[ks]) return ks;
+  }
+  return 1;
+}
+
 template <int BN, int STAGES, int EPI>
 static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit,
                                const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t stream) {
@@ -396,7 +406,9 @@ static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int
   const int n_tiles = (N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
   const int kblocks = (K + kBK - 1) / kBK;
-  if (ksplit <= 0) ksplit = choose_ksplit(kern, C::kSmemBytes, tiles, kblocks);
+  static int cap[9] = {0};  // clusters of each size this instantiation fits on the device, filled on first use
+  if (ksplit == 0) ksplit = choose_ksplit(kern, C::kSmemBytes, tiles, kblocks, cap);
+  if (ksplit < 0) ksplit = one_wave_ksplit(kern, C::kSmemBytes, tiles, std::min(-ksplit, kblocks), cap);
   ksplit = std::max(1, std::min(ksplit, std::min(8, kblocks)));
   const int group_m = std::min(16, m_tiles);
   cudaLaunchConfig_t cfg = {};
@@ -460,15 +472,26 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   if (!ep.a_tiled && (e = make_tmap(&ta, A, M, K, lda, kBM)) != cudaSuccess) return e;
   if (!ep.b_tiled && (e = make_tmap(&tb, B, N, K, ldb, BN)) != cudaSuccess) return e;
   // GEMMs whose A operand is a pre-tiled weight matrix (the decode projections) stream that matrix from
-  // HBM: one CTA per SM with a ~190 KB ring in flight, split-K only as far as the whole launch stays one
-  // wave, so no CTA waits for another to finish before it starts streaming.  Other skinny tiles use a
-  // 3-stage ring (< 75 KB) so three CTAs share an SM; wide tiles take the SM.
+  // HBM with ~190 KB in flight per SM and split-K only as far as the whole launch stays one wave, so no CTA
+  // waits for another to finish before it starts streaming: one CTA per SM with an 8-stage ring, or, for
+  // launches of more tiles than SMs (wide tensor-parallel batches), two CTAs per SM with 4-stage rings.
+  // (Two 4-stage CTAs per SM with a deeper split measured slower than one 8-stage CTA for in_proj.)
+  // Other skinny tiles use a 3-stage ring (< 75 KB) so three CTAs share an SM; wide tiles take the SM.
   if (ep.a_tiled) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-    if (ksplit <= 0) ksplit = std::max(1, std::min(8, sms / tiles));
+    const int k1 = sms / tiles;
+    const bool two_per_sm = ksplit <= 0 && k1 == 0;
+    if (ksplit <= 0) ksplit = -std::max(1, std::min(8, two_per_sm ? 2 * sms / tiles : k1));  // < 0: one wave
+    if (two_per_sm) {
+      switch (BN) {  // rings of 4 stages, up to 4 x 24 KB
+        case 16: return dispatch_epi<16, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+        case 32: return dispatch_epi<32, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+        default: return dispatch_epi<64, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+      }
+    }
     switch (BN) {  // rings of 8 stages, up to 8 x 24 KB
       case 16: return dispatch_epi<16, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
       case 32: return dispatch_epi<32, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
