@@ -104,6 +104,14 @@ GDN_API gdn_status gdn_layer_get_info(const gdn_layer* layer, gdn_layer_info* in
  * allocate nothing (required before capturing forwards into a CUDA graph). */
 GDN_API gdn_status gdn_layer_reserve(gdn_layer* layer, int64_t max_tokens);
 
+/* `layer` drops its own workspace and from now on uses `owner`'s (reference counted; it grows to the largest
+ * call any sharer makes), so that the layers of a stack hold one workspace between them instead of one each
+ * (a 24-layer stack prefilling 128 x 4096 tokens needs ~40 GB of intermediates once, not 24 times).  Sharers
+ * must issue their calls on one stream.  The reference's stack owns one constants tensor and one set of
+ * work buffers for all its layers (0.8B/gdn_l1.py:186-190, 214-221); this is the device-memory counterpart
+ * (there is no separate reference call). */
+GDN_API gdn_status gdn_layer_share_workspace(gdn_layer* layer, gdn_layer* owner);
+
 /* One layer call that continues from (rec_state, conv_state) and updates both in place:
  *   T == 1  decode step (one token per sequence);  T > 1  chunked prefill of T tokens per sequence.
  * out receives the layer output (bf16 [B, T, hidden]); with tp_size > 1 every rank receives the full,

@@ -23,7 +23,7 @@ EXPORTED = (
     "gdn_layer_create", "gdn_layer_destroy", "gdn_layer_get_info", "gdn_layer_reserve", "gdn_layer_forward",
     "gdn_recurrence_forward", "gdn_comm_get_unique_id", "gdn_comm_create", "gdn_comm_destroy",
     "gdn_device_error", "gdn_last_error_string", "gdn_kernel_launch_count", "gdn_abi_version", "gdn_gemm_bf16",
-    "gdn_layer_set_stage_events", "gdn_layer_decode_static",
+    "gdn_layer_set_stage_events", "gdn_layer_decode_static", "gdn_layer_share_workspace",
 )
 
 
@@ -78,6 +78,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gdn_gemm_bf16": [P, I64, P, I64, I32, I32, I32, I32, P, I64, I32, P],
         "gdn_layer_set_stage_events": [P, ctypes.POINTER(P), I32],
         "gdn_layer_decode_static": [P, P, I32, P, P, P, P],
+        "gdn_layer_share_workspace": [P, P],
     }
     for name, args in sigs.items():
         fn = getattr(lib, name)

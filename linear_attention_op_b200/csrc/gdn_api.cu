@@ -159,6 +159,15 @@ static void p2p_teardown(gdn_comm* c) {
 // ------------------------------------------------------------------------------------------------
 // Layer
 // ------------------------------------------------------------------------------------------------
+// Device workspace for the intermediates of a call.  Layers that issue their calls on one stream (the
+// layers of a stack) may share one (gdn_layer_share_workspace): it is reference counted and grows to the
+// largest call any of them makes, so a stack of L layers holds one prefill workspace instead of L.
+struct WsBlock {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int refs = 1;
+};
+
 struct gdn_layer {
   gdn_dims dims{};
   int tp_rank = 0, tp_size = 1;
@@ -173,8 +182,7 @@ struct gdn_layer {
   float* a_log = nullptr;           // [hv]
   float* dt_bias = nullptr;         // [hv]
   float* norm_w = nullptr;          // [128]
-  void* ws = nullptr;
-  size_t ws_bytes = 0;
+  WsBlock* ws = nullptr;            // never null after gdn_layer_create
   cudaEvent_t stage_events[7] = {};  // optional stage timing (gdn_layer_set_stage_events)
   int n_stage_events = 0;
 };
@@ -198,26 +206,34 @@ static WsLayout ws_layout(const gdn_layer* L, int64_t n, int64_t chunks) {
 static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks) { return ws_layout(L, n, chunks).total; }
 static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream) {
   const size_t need = workspace_bytes(L, n, chunks);
-  if (need <= L->ws_bytes) return GDN_OK;
+  WsBlock* w = L->ws;
+  if (need <= w->bytes) return GDN_OK;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
     return fail(GDN_ERR_INVALID_ARGUMENT,
                 "workspace for %lld rows is not reserved; call gdn_layer_reserve before stream capture",
                 static_cast<long long>(n));
-  if (L->ws) GDN_CUDA(cudaFree(L->ws));
-  L->ws = nullptr;
-  L->ws_bytes = 0;
-  GDN_CUDA(cudaMalloc(&L->ws, need));
-  L->ws_bytes = need;
+  if (w->ptr) GDN_CUDA(cudaFree(w->ptr));  // synchronises: no sharer's call still uses the old block
+  w->ptr = nullptr;
+  w->bytes = 0;
+  GDN_CUDA(cudaMalloc(&w->ptr, need));
+  w->bytes = need;
   return GDN_OK;
+}
+
+static void release_ws(WsBlock* w) {
+  if (w && --w->refs == 0) {
+    if (w->ptr) cudaFree(w->ptr);
+    delete w;
+  }
 }
 
 static void free_layer(gdn_layer* L) {
   if (!L) return;
   for (void* p : {static_cast<void*>(L->w_in), static_cast<void*>(L->w_out), static_cast<void*>(L->conv_w),
-                  static_cast<void*>(L->a_log), static_cast<void*>(L->dt_bias), static_cast<void*>(L->norm_w),
-                  L->ws})
+                  static_cast<void*>(L->a_log), static_cast<void*>(L->dt_bias), static_cast<void*>(L->norm_w)})
     if (p) cudaFree(p);
+  release_ws(L->ws);
   delete L;
 }
 
@@ -258,6 +274,11 @@ extern "C" gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* 
 
   gdn_layer* L = new (std::nothrow) gdn_layer();
   if (!L) return fail(GDN_ERR_OUT_OF_MEMORY, "host allocation failed");
+  L->ws = new (std::nothrow) WsBlock();
+  if (!L->ws) {
+    delete L;
+    return fail(GDN_ERR_OUT_OF_MEMORY, "host allocation failed");
+  }
   L->dims = d;
   L->tp_rank = tp_rank;
   L->tp_size = tp_size;
@@ -339,7 +360,7 @@ extern "C" gdn_status gdn_layer_get_info(const gdn_layer* L, gdn_layer_info* inf
   info->tp_size = L->tp_size;
   info->rec_state_floats_per_seq = static_cast<int64_t>(L->hv) * kHeadDim * kHeadDim;
   info->conv_state_floats_per_seq = 3LL * L->conv_dim;
-  info->workspace_bytes = static_cast<int64_t>(L->ws_bytes);
+  info->workspace_bytes = static_cast<int64_t>(L->ws->bytes);
   return GDN_OK;
 }
 
@@ -348,6 +369,17 @@ extern "C" gdn_status gdn_layer_reserve(gdn_layer* L, int64_t max_tokens) {
   if (max_tokens <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens must be > 0");
   // prefill chunks: B * ceil(T / 64) <= max_tokens / 64 + B; room for up to 64 ragged sequences
   return ensure_workspace(L, max_tokens, max_tokens / 64 + 64, nullptr);
+}
+
+extern "C" gdn_status gdn_layer_share_workspace(gdn_layer* L, gdn_layer* owner) {
+  if (!L || !owner) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_share_workspace: null layer");
+  if (L->device != owner->device)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "layers live on devices %d and %d", L->device, owner->device);
+  if (L->ws == owner->ws) return GDN_OK;
+  release_ws(L->ws);
+  L->ws = owner->ws;
+  ++L->ws->refs;
+  return GDN_OK;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -438,7 +470,7 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   gdn_status st = ensure_workspace(L, n, chunks, stream);
   if (st != GDN_OK) return st;
   const int h = L->dims.hidden;
-  char* ws = static_cast<char*>(L->ws);
+  char* ws = static_cast<char*>(L->ws->ptr);
   const WsLayout lay = ws_layout(L, n, chunks);
   float* proj = reinterpret_cast<float*>(ws);
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + lay.y);

@@ -207,6 +207,16 @@ class Qwen35GatedDeltaNet:
         with torch.cuda.device(self.device):
             self._h.reserve(max_tokens)
 
+    def share_workspace(self, owner: "Qwen35GatedDeltaNet") -> None:
+        """Use owner's device workspace instead of this layer's own (gdn_layer_share_workspace); the two
+        must then run on one stream."""
+        call("gdn_layer_share_workspace", self._h.handle, owner._h.handle)
+
+    def workspace_bytes(self) -> int:
+        info = LayerInfo()
+        call("gdn_layer_get_info", self._h.handle, ctypes.byref(info))
+        return int(info.workspace_bytes)
+
     def with_batch(self, batch: int) -> "Qwen35GatedDeltaNet":
         """Another op over the same device weights (and workspace) with its own batch size and zeroed state.
         The two ops must not run concurrently on different streams (they share the workspace)."""
@@ -235,14 +245,20 @@ class GDNStack:
     """Several GDN layers run back to back, each with its own state (decode or prefill).
 
     Drop-in for ``Qwen35_08B_GDNStackL1(device, hf_layers, batch)``: ``stack(x, layers=None)`` applies the
-    selected layers in order (GDN mixers only: no norms, residuals or MLP, like the reference)."""
+    selected layers in order (GDN mixers only: no norms, residuals or MLP, like the reference).  The layers
+    run on one stream and share one device workspace (sized by the largest call), as the reference's stack
+    shares its scratch buffers."""
 
     def __init__(self, hf_layers, batch: int = 1, *, device=None, tp_rank: int = 0, tp_size: int = 1, comm=None,
                  max_rows: int | None = None):
         self.batch = batch
         self.layers = [Qwen35GatedDeltaNet(weights=LayerWeights.from_any(L), batch=batch, device=device,
-                                           tp_rank=tp_rank, tp_size=tp_size, comm=comm, max_rows=max_rows)
+                                           tp_rank=tp_rank, tp_size=tp_size, comm=comm)
                        for L in hf_layers]
+        for L in self.layers[1:]:
+            L.share_workspace(self.layers[0])
+        if max_rows:
+            self.layers[0].reserve(max_rows)
         self.hidden = self.layers[0].hidden
         self.device = self.layers[0].device
 

@@ -1,0 +1,98 @@
+"""Config 4 of the benchmark spec: a stack of Qwen3.5-9B-shaped GDN layers (per-layer seeds, strong decay
+A_log = log U(1, 64)), prefill then decode -- the reference's stacked decode loop (0.8B/gdn_l1.py:295-325,
+0.8B/bench_decode.py:44-60) at the 9B geometry.
+
+* At test size against the CPU oracle: 3 layers, batch 2, 150-token prefill then 4 decode steps, every
+  layer's output (on the input that layer received) and final state.
+* At full size (24 layers, batch 128, 4096-token prefill, 512 decode steps) through size-independent
+  properties: the layers share one workspace (24 separate prefill workspaces of ~40 GB would not fit), every
+  output is finite, and two sequences of the batch-128 run equal the same two sequences run as a batch of 2.
+"""
+import pytest
+import torch
+
+from linear_attention_op_b200 import GDNStack, LayerWeights, device_error
+from oracle import gdn_oracle as O
+from tests._util import STATE_TOL, check, requires_b200
+
+pytestmark = [pytest.mark.gpu, requires_b200]
+
+H, HK, HV = 4096, 16, 32
+
+
+def test_config4_stack_at_test_size_vs_oracle():
+    """Each layer of the stack against the oracle on the input that layer received on the device (the
+    previous layer's bf16 output), prefill and then every decode step, and every layer's final state."""
+    ws = [O.make_weights(H, HK, HV, seed=100 + i, a_max=64.0) for i in range(3)]
+    B, t0, steps = 2, 150, 4
+    x = O.make_hidden(B, t0 + steps, H, seed=99)
+    stack = GDNStack(ws, batch=B)
+    states = []
+    cur = x[:, :t0]
+    for i, w in enumerate(ws):
+        got = stack(cur, layers=[i])
+        want, s, c = O.layer_forward(w, cur, mode="chunk")
+        check(f"cfg4 layer {i} prefill out", got, want)
+        states.append((s, c))
+        cur = got.float()  # bf16 values, exact in fp32
+    for t in range(steps):
+        cur = x[:, t0 + t:t0 + t + 1]
+        for i, w in enumerate(ws):
+            got = stack(cur, layers=[i])
+            want, s, c = O.layer_forward(w, cur, *states[i], mode="recurrent")
+            check(f"cfg4 layer {i} decode step {t} out", got, want)
+            states[i] = (s, c)
+            cur = got.float()
+    assert device_error() == 0
+    for i in range(3):
+        check(f"cfg4 layer {i} state", stack.get_recurrent_state(i), states[i][0], max_rel=STATE_TOL)
+
+
+def _device_layer(seed: int, device) -> LayerWeights:
+    """The spec's distributions for one 9B-shaped layer, generated on the device."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    conv_dim, vd = 2 * HK * 128 + HV * 128, HV * 128
+    rn = lambda *s: (torch.randn(*s, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return LayerWeights(
+        w_qkv=rn(conv_dim, H), w_z=rn(vd, H), w_a=rn(HV, H), w_b=rn(HV, H),
+        conv_w=((torch.rand(conv_dim, 4, generator=g, device=device) * 2 - 1) * 0.5).bfloat16().float(),
+        a_log=torch.log(1 + torch.rand(HV, generator=g, device=device) * 63.0),
+        dt_bias=torch.randn(HV, generator=g, device=device) * 0.1,
+        norm_w=0.5 + torch.rand(128, generator=g, device=device),
+        w_out=rn(H, vd), num_k_heads=HK, num_v_heads=HV)
+
+
+def test_config4_full_size_batch_independence_and_shared_workspace():
+    dev = torch.device("cuda", 0)
+    L, B, T0, steps, pick = 24, 128, 4096, 512, [0, 101]
+    weights = [_device_layer(1000 + i, dev) for i in range(L)]
+    g = torch.Generator(device=dev).manual_seed(7)
+    x_pre = torch.randn(B, T0, H, generator=g, device=dev).to(torch.bfloat16)
+    x_dec = torch.randn(steps, B, 1, H, generator=g, device=dev).to(torch.bfloat16)
+
+    big = GDNStack(weights, batch=B, device=dev)
+    y_big = big(x_pre)
+    sizes = {layer.workspace_bytes() for layer in big.layers}
+    assert len(sizes) == 1 and sizes.pop() > 20 * 2**30, "one shared prefill workspace"
+    assert torch.isfinite(y_big.float()).all()
+    y_big_pre = y_big[pick].float().cpu()
+    del y_big
+    last_big = None
+    for t in range(steps):
+        last_big = big(x_dec[t])
+    assert device_error() == 0
+    assert torch.isfinite(last_big.float()).all()
+    last_big = last_big[pick].float().cpu()
+    s_big = [big.get_recurrent_state(i)[pick] for i in (0, L // 2, L - 1)]
+    del big
+
+    small = GDNStack(weights, batch=len(pick), device=dev)
+    y_small = small(x_pre[pick]).float().cpu()
+    last_small = None
+    for t in range(steps):
+        last_small = small(x_dec[t][pick])
+    assert device_error() == 0
+    check("cfg4 prefill, 2 of 128 vs alone", y_big_pre, y_small)
+    check("cfg4 decode step 512, 2 of 128 vs alone", last_big, last_small.float().cpu())
+    for j, i in enumerate((0, L // 2, L - 1)):
+        check(f"cfg4 layer {i} state, 2 of 128 vs alone", s_big[j], small.get_recurrent_state(i), max_rel=STATE_TOL)
