@@ -6,7 +6,8 @@ A_log = log U(1, 64)), prefill then decode -- the reference's stacked decode loo
   layer's output (on the input that layer received) and final state.
 * At full size (24 layers, batch 128, 4096-token prefill, 512 decode steps) through size-independent
   properties: the layers share one workspace (24 separate prefill workspaces of ~40 GB would not fit), every
-  output is finite, and two sequences of the batch-128 run equal the same two sequences run as a batch of 2.
+  output is finite, and two sequences of the batch-128 run equal the same two sequences run as a batch of 2
+  (outputs and states of the layers whose activations have not yet vanished).
 """
 import pytest
 import torch
@@ -63,36 +64,52 @@ def _device_layer(seed: int, device) -> LayerWeights:
 
 
 def test_config4_full_size_batch_independence_and_shared_workspace():
+    """A stack of GDN mixers alone (no residual, no norms, as in the reference's stack) shrinks its
+    activations layer by layer -- the oracle gives RMS 0.78, 0.54, 0.28, 0.087, 0.010 after layers 0-4 and
+    exact zeros from layer 8 on -- so the comparisons use layers 0-3, where the values are O(0.1-1).  Each
+    of those layers is rerun for two of the 128 sequences as a batch of 2, on exactly the inputs it received
+    in the batch-128 run: its prefill output, its output at the last of the 512 decode steps and its final
+    state must match (the batch size changes only the decode out_proj's split-K order)."""
     dev = torch.device("cuda", 0)
     L, B, T0, steps, pick = 24, 128, 4096, 512, [0, 101]
+    layers = (0, 1, 2, 3)
     weights = [_device_layer(1000 + i, dev) for i in range(L)]
     g = torch.Generator(device=dev).manual_seed(7)
     x_pre = torch.randn(B, T0, H, generator=g, device=dev).to(torch.bfloat16)
     x_dec = torch.randn(steps, B, 1, H, generator=g, device=dev).to(torch.bfloat16)
 
     big = GDNStack(weights, batch=B, device=dev)
-    y_big = big(x_pre)
+    inputs = {i: [] for i in layers}  # the picked rows of every input layer i received: prefill, then steps
+    pre_big, dec_big = {}, {}
+    cur = x_pre
+    for i in range(L):
+        if i in layers:
+            inputs[i].append(cur[pick].clone())
+        cur = big(cur, layers=[i])
+        assert torch.isfinite(cur).all(), f"layer {i} prefill"
+        if i in layers:
+            pre_big[i] = cur[pick].float().cpu()
     sizes = {layer.workspace_bytes() for layer in big.layers}
     assert len(sizes) == 1 and sizes.pop() > 20 * 2**30, "one shared prefill workspace"
-    assert torch.isfinite(y_big.float()).all()
-    y_big_pre = y_big[pick].float().cpu()
-    del y_big
-    last_big = None
     for t in range(steps):
-        last_big = big(x_dec[t])
+        cur = x_dec[t]
+        for i in range(L):
+            if i in layers:
+                inputs[i].append(cur[pick].clone())
+            cur = big(cur, layers=[i])
+            if t == steps - 1 and i in layers:
+                dec_big[i] = cur[pick].float().cpu()
+    assert torch.isfinite(cur).all()
     assert device_error() == 0
-    assert torch.isfinite(last_big.float()).all()
-    last_big = last_big[pick].float().cpu()
-    s_big = [big.get_recurrent_state(i)[pick] for i in (0, L // 2, L - 1)]
+    s_big = {i: big.get_recurrent_state(i)[pick] for i in layers}
     del big
 
-    small = GDNStack(weights, batch=len(pick), device=dev)
-    y_small = small(x_pre[pick]).float().cpu()
-    last_small = None
-    for t in range(steps):
-        last_small = small(x_dec[t][pick])
+    small = GDNStack(weights[:len(layers)], batch=len(pick), device=dev)
+    for i in layers:
+        y = small(inputs[i][0], layers=[i])
+        check(f"cfg4 layer {i} prefill, 2 of 128 vs alone", pre_big[i], y)
+        for t in range(steps):
+            y = small(inputs[i][1 + t], layers=[i])
+        check(f"cfg4 layer {i} decode step {steps}, 2 of 128 vs alone", dec_big[i], y)
+        check(f"cfg4 layer {i} state, 2 of 128 vs alone", s_big[i], small.get_recurrent_state(i), max_rel=STATE_TOL)
     assert device_error() == 0
-    check("cfg4 prefill, 2 of 128 vs alone", y_big_pre, y_small)
-    check("cfg4 decode step 512, 2 of 128 vs alone", last_big, last_small.float().cpu())
-    for j, i in enumerate((0, L // 2, L - 1)):
-        check(f"cfg4 layer {i} state, 2 of 128 vs alone", s_big[j], small.get_recurrent_state(i), max_rel=STATE_TOL)
