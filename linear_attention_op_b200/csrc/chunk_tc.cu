@@ -313,19 +313,33 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
       gi[kC + gtid] = gE[gtid];
       gi[2 * kC + gtid] = gC[gtid];
     }
+    // Warps q4 = 0 and 2 hold rows 0..31, whose columns 32..63 are above the diagonal: M's there are never
+    // read (the inverse reads only entries below the diagonal; W later lives in that quarter) and A's are
+    // zeros, written without computing their exps.
     const float Gt = gG[t_row];
+    const bool hi_rows = q4 & 1;
     if (is_k) {
       const float bt = gB[t_row];
+      float* mrow = gm + t_row * kLdF;
 #pragma unroll
-      for (int s = 0; s < kC; ++s) gm[t_row * kLdF + s] = s < t_row ? bt * acc[s] * __expf(Gt - gG[s]) : 0.f;
+      for (int s = 0; s < 32; ++s) mrow[s] = s < t_row ? bt * acc[s] * __expf(Gt - gG[s]) : 0.f;
+      if (hi_rows) {
+#pragma unroll
+        for (int s = 32; s < kC; ++s) mrow[s] = s < t_row ? bt * acc[s] * __expf(Gt - gG[s]) : 0.f;
+      }
     } else {
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float av[8];
+        if (c8 < 4 || hi_rows) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int s = 8 * c8 + i;
-          av[i] = s <= t_row ? acc[s] * __expf(Gt - gG[s]) : 0.f;
+          for (int i = 0; i < 8; ++i) {
+            const int s = 8 * c8 + i;
+            av[i] = s <= t_row ? acc[s] * __expf(Gt - gG[s]) : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) av[i] = 0.f;
         }
         uint4 hi, lo;
         pack8(av, hi, lo);

@@ -29,6 +29,26 @@ def _stream_handle(stream: torch.cuda.Stream | None = None) -> ctypes.c_void_p:
     return ctypes.c_void_p(s.cuda_stream)
 
 
+def _to_device(t: torch.Tensor, device: torch.device) -> tuple[torch.Tensor, bool]:
+    """Contiguous bf16 copy of t on device; a pinned host tensor is copied without blocking the host
+    (the caller synchronises before it returns)."""
+    pinned = t.device.type == "cpu" and t.is_pinned()
+    return t.to(device=device, dtype=torch.bfloat16, non_blocking=pinned).contiguous(), pinned
+
+
+def _to_caller(out: torch.Tensor, like: torch.Tensor, pinned: bool) -> torch.Tensor:
+    """out (device bf16) in like's device and dtype.  For a pinned host input the result comes back into
+    pinned host memory (a direct DMA, where a pageable destination would be staged) and the current stream
+    is synchronised before returning."""
+    if not pinned:
+        return out.to(device=like.device, dtype=like.dtype)
+    src = out if like.dtype == out.dtype else out.to(like.dtype)
+    res = torch.empty(src.shape, dtype=src.dtype, pin_memory=True)
+    res.copy_(src, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+    return res
+
+
 def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
@@ -198,10 +218,10 @@ class Qwen35GatedDeltaNet:
         if B != self.batch or H != self.hidden:
             raise ValueError(f"hidden_states is {tuple(hidden_states.shape)}, layer expects [{self.batch}, T, {self.hidden}]")
         with torch.cuda.device(self.device):
-            x = hidden_states.to(device=self.device, dtype=torch.bfloat16).contiguous()
+            x, pinned = _to_device(hidden_states, self.device)
             out = torch.empty_like(x)
             self.forward_into(x, out)
-        return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
+            return _to_caller(out, hidden_states, pinned)
 
     def reserve(self, max_tokens: int) -> None:
         with torch.cuda.device(self.device):
@@ -285,12 +305,12 @@ class GDNStack:
         x = hidden_states.reshape(self.batch, -1, shape[-1])
         idx = range(len(self.layers)) if layers is None else layers
         with torch.cuda.device(self.device):
-            cur = x.to(device=self.device, dtype=torch.bfloat16).contiguous()
+            cur, pinned = _to_device(x, self.device)
             for i in idx:
                 out = torch.empty_like(cur)
                 self.layers[i].forward_into(cur, out)
                 cur = out
-        return cur.reshape(shape).to(device=hidden_states.device, dtype=hidden_states.dtype)
+            return _to_caller(cur, hidden_states, pinned).reshape(shape)
 
 
 class GatedDeltaRule:
