@@ -74,12 +74,13 @@ def synthetic_weights(seed: int, device, a_max: float = 16.0):
         w_out=rn(H, vd), num_k_heads=HK, num_v_heads=HV)
 
 
-def decode_bytes(B: int, world: int = 1) -> dict:
-    """Algorithmic HBM bytes of one decode step (the per-unit figures of the design notes), per GPU."""
+def decode_bytes(B: int, world: int = 1, wbytes: int = 2) -> dict:
+    """Algorithmic HBM bytes of one decode step (the per-unit figures of the design notes), per GPU;
+    wbytes = bytes per weight (2 bf16, 1 with fp8 weights)."""
     hv, kd, vd = HV // world, HK * D // world, HV * D // world
     conv_dim = 2 * kd + vd
     rows = conv_dim + vd + 2 * hv
-    w_in, w_out = rows * H * 2, H * vd * 2
+    w_in, w_out = rows * H * wbytes, H * vd * wbytes
     state = 2 * B * hv * D * D * 4
     conv = 2 * B * conv_dim * 3 * 4
     act = 2 * B * H * 2
@@ -243,7 +244,8 @@ def run_ours(args):
     W = synthetic_weights(0, dev)
     B = DECODE_B * world  # 64 sequences per GPU: each GPU holds all of them for its 1/N of the heads
     layer = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev, tp_rank=rank, tp_size=world, comm=comm,
-                                max_rows=max(B, PREFILL_B * PREFILL_T if args.prefill else B))
+                                max_rows=max(B, PREFILL_B * PREFILL_T if args.prefill else B),
+                                weight_dtype=args.weights)
     if args.only == "prefill":  # profiling case: the prefill workload alone
         res = run_prefill(args, layer, dev, world, pk, traffic)
         if rank == 0:
@@ -305,7 +307,7 @@ def run_ours(args):
 
     st = stage_times(layer, dec_step, min(args.steps, 50))
     names = STAGES
-    byt = decode_bytes(B, world)
+    byt = decode_bytes(B, world, 1 if args.weights == "fp8" else 2)
     dec_stage = {n: round(t * 1e3, 2) for n, t in zip(names, st) if n not in ("conv", "chunk_prep")}
     dom = max(["in_proj", "recurrence", "out_proj"], key=lambda n: dec_stage[n])
     achieved = byt[dom] / (dec_stage[dom] * 1e-6) / 1e9
@@ -339,7 +341,8 @@ def run_ours(args):
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 (fp32 state, fp32 accumulation)", "data": "synthetic",
+        "vs_baseline": None, "dtype": ("bf16 (fp32 state, fp32 accumulation)" if args.weights == "bf16" else
+                  "fp8 e4m3 projection weights and decode activations, bf16 elsewhere (fp32 state, fp32 accumulation)"), "data": "synthetic",
         "config": {"workload": f"cfg2: Qwen3.5-9B GDN layer decode, batch {DECODE_B} per GPU (global {B}), "
                                "fp32 state ~N(0,0.1)",
                    "model": "Qwen3.5-9B GDN layer (random init)", "global_batch": B, "seq_len": 1,
@@ -480,6 +483,9 @@ def main():
     ap.add_argument("--graph-steps", type=int, default=16, help="decode steps captured per CUDA graph")
     ap.add_argument("--prefill-b", type=int, default=PREFILL_B)
     ap.add_argument("--prefill-t", type=int, default=PREFILL_T)
+    ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
+                    help="fp8: e4m3 projection weights and decode activations (not the benchmark config's "
+                         "bf16 weights; reported beside it)")
     args = ap.parse_args()
     globals()["DECODE_B"], globals()["PREFILL_B"], globals()["PREFILL_T"] = args.decode_b, args.prefill_b, args.prefill_t
     if args.only == "decode":

@@ -112,6 +112,21 @@ GDN_API gdn_status gdn_layer_reserve(gdn_layer* layer, int64_t max_tokens);
  * (there is no separate reference call). */
 GDN_API gdn_status gdn_layer_share_workspace(gdn_layer* layer, gdn_layer* owner);
 
+/* Weight formats (the reference's weight_dtype argument: ttnn.bfloat16 / bfloat8_b, 9B/gdn_layer.py:55,90-119,
+ * 0.8B/gdn_l1.py:155). */
+enum {
+  GDN_WEIGHTS_BF16 = 0,     /* as created */
+  GDN_WEIGHTS_FP8_E4M3 = 1  /* e4m3 weights with one power-of-two scale per output row */
+};
+
+/* Switch a layer's projection weights to `format`.  GDN_WEIGHTS_FP8_E4M3 quantises every output row of the
+ * fused in_proj and of out_proj to e4m3 with the smallest power-of-two scale that keeps the row within
+ * +-448; decode calls (T == 1) then quantise their activations the same way per token and run the
+ * projections as e4m3 x e4m3 tensor-core GEMMs (half the weight bytes streamed per step), and prefill calls
+ * use the dequantised weights (exact in bf16) with bf16 activations.  One way: the bf16 originals are not
+ * kept.  tp_size 1 only; gdn_layer_decode_static is unavailable for fp8 layers. */
+GDN_API gdn_status gdn_layer_set_weight_format(gdn_layer* layer, int32_t format);
+
 /* One layer call that continues from (rec_state, conv_state) and updates both in place:
  *   T == 1  decode step (one token per sequence);  T > 1  chunked prefill of T tokens per sequence.
  * out receives the layer output (bf16 [B, T, hidden]); with tp_size > 1 every rank receives the full,

@@ -182,6 +182,13 @@ struct gdn_layer {
   float* a_log = nullptr;           // [hv]
   float* dt_bias = nullptr;         // [hv]
   float* norm_w = nullptr;          // [128]
+  // fp8 weights (gdn_layer_set_weight_format): e4m3 copies of w_in / w_out in the streaming layout with
+  // 128-element K blocks and their per-row power-of-two scales; w_in / w_out then hold the dequantised
+  // values, which the bf16 (prefill) GEMMs use.
+  uint8_t* w_in8 = nullptr;
+  uint8_t* w_out8 = nullptr;
+  float* s_in = nullptr;            // [rows]
+  float* s_out = nullptr;           // [hidden]
   WsBlock* ws = nullptr;            // never null after gdn_layer_create
   cudaEvent_t stage_events[7] = {};  // optional stage timing (gdn_layer_set_stage_events)
   int n_stage_events = 0;
@@ -191,21 +198,28 @@ static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Workspace layout for n token rows in `chunks` (sequence, chunk) pairs (chunks >= B for prefill):
 //   proj fp32 [n, proj_ld] (conv channels already convolved) | y bf16 [n, vd] |
-//   conv tail fp32 [chunks, 3, conv_dim] | chunk tile images
+//   conv tail fp32 [chunks, 3, conv_dim] | chunk tile images | (fp8 decode) e4m3 x [n, hidden], x scales
+//   [n], e4m3 y [n, vd], y scales [n]
 struct WsLayout {
-  size_t y, tail, chunk, total;
+  size_t y, tail, chunk, q8, total;
 };
-static WsLayout ws_layout(const gdn_layer* L, int64_t n, int64_t chunks) {
+static size_t q8_bytes(const gdn_layer* L, int64_t n) {
+  return align256(n * L->dims.hidden) + align256(n * 4) + align256(n * L->vd) + align256(n * 4);
+}
+static WsLayout ws_layout(const gdn_layer* L, int64_t n, int64_t chunks, bool f8 = false) {
   WsLayout o;
   o.y = align256(n * L->proj_ld * 4);
   o.tail = o.y + align256(n * L->vd * 2);
   o.chunk = o.tail + align256(static_cast<size_t>(chunks) * 3 * L->conv_dim * 4);
-  o.total = o.chunk + align256(chunk_prefill_scratch_bytes(1, 64, L->hk, L->hv) * static_cast<size_t>(chunks));
+  o.q8 = o.chunk + align256(chunk_prefill_scratch_bytes(1, 64, L->hk, L->hv) * static_cast<size_t>(chunks));
+  o.total = o.q8 + (f8 ? q8_bytes(L, n) : 0);
   return o;
 }
-static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks) { return ws_layout(L, n, chunks).total; }
-static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream) {
-  const size_t need = workspace_bytes(L, n, chunks);
+static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks, bool f8) {
+  return ws_layout(L, n, chunks, f8).total;
+}
+static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream, bool f8 = false) {
+  const size_t need = workspace_bytes(L, n, chunks, f8);
   WsBlock* w = L->ws;
   if (need <= w->bytes) return GDN_OK;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -231,7 +245,9 @@ static void release_ws(WsBlock* w) {
 static void free_layer(gdn_layer* L) {
   if (!L) return;
   for (void* p : {static_cast<void*>(L->w_in), static_cast<void*>(L->w_out), static_cast<void*>(L->conv_w),
-                  static_cast<void*>(L->a_log), static_cast<void*>(L->dt_bias), static_cast<void*>(L->norm_w)})
+                  static_cast<void*>(L->a_log), static_cast<void*>(L->dt_bias), static_cast<void*>(L->norm_w),
+                  static_cast<void*>(L->w_in8), static_cast<void*>(L->w_out8), static_cast<void*>(L->s_in),
+                  static_cast<void*>(L->s_out)})
     if (p) cudaFree(p);
   release_ws(L->ws);
   delete L;
@@ -368,7 +384,29 @@ extern "C" gdn_status gdn_layer_reserve(gdn_layer* L, int64_t max_tokens) {
   if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_reserve: null layer");
   if (max_tokens <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens must be > 0");
   // prefill chunks: B * ceil(T / 64) <= max_tokens / 64 + B; room for up to 64 ragged sequences
-  return ensure_workspace(L, max_tokens, max_tokens / 64 + 64, nullptr);
+  return ensure_workspace(L, max_tokens, max_tokens / 64 + 64, nullptr, L->w_in8 != nullptr);
+}
+
+extern "C" gdn_status gdn_layer_set_weight_format(gdn_layer* L, int32_t format) {
+  if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_set_weight_format: null layer");
+  if (format == GDN_WEIGHTS_BF16)
+    return L->w_in8 ? fail(GDN_ERR_UNSUPPORTED, "the weights are fp8 already (the bf16 originals are not kept)")
+                    : GDN_OK;
+  if (format != GDN_WEIGHTS_FP8_E4M3) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown weight format %d", format);
+  if (L->w_in8) return GDN_OK;
+  if (L->tp_size > 1)
+    return fail(GDN_ERR_UNSUPPORTED, "fp8 weights need tp_size 1 (out_proj row scales would differ per shard)");
+  const int h = L->dims.hidden;
+  if (h % 128 || L->vd % 128)
+    return fail(GDN_ERR_UNSUPPORTED, "fp8 weights need hidden and value width multiples of 128");
+  GDN_CUDA(cudaMalloc(&L->w_in8, tiled_weight_bytes(L->rows, h) / 2));
+  GDN_CUDA(cudaMalloc(&L->w_out8, tiled_weight_bytes(h, L->vd) / 2));
+  GDN_CUDA(cudaMalloc(&L->s_in, static_cast<size_t>(L->rows) * 4));
+  GDN_CUDA(cudaMalloc(&L->s_out, static_cast<size_t>(h) * 4));
+  GDN_CUDA(quantize_tiled_weights_fp8(L->w_in, L->rows, h, L->w_in8, L->s_in, nullptr));
+  GDN_CUDA(quantize_tiled_weights_fp8(L->w_out, h, L->vd, L->w_out8, L->s_out, nullptr));
+  GDN_CUDA(cudaDeviceSynchronize());
+  return GDN_OK;
 }
 
 extern "C" gdn_status gdn_layer_share_workspace(gdn_layer* L, gdn_layer* owner) {
@@ -401,9 +439,12 @@ extern "C" gdn_status gdn_layer_set_stage_events(gdn_layer* L, void* const* even
 // conv + conv-state roll + gated delta rule + gated RMSNorm (decode_step_kernel, which loads the state
 // and the conv history while the GEMM runs) -> out_proj, chained by programmatic dependent launch.
 // proj [B, proj_ld] fp32 and y [B, vd] bf16 are scratch.
+// q8: with fp8 weights, the workspace region for the e4m3 activations and their scales (q8_bytes); the
+// projections then run as quantize_rows_fp8 + gemm_f8_tn.
 static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* rec_state, float* conv_state,
                                float* proj, __nv_bfloat16* y, uint16_t* out, cudaStream_t stream, bool marks,
-                               const unsigned long long* slot_epoch = nullptr, int64_t slot_bytes = 0) {
+                               const unsigned long long* slot_epoch = nullptr, int64_t slot_bytes = 0,
+                               void* q8 = nullptr) {
   const int h = L->dims.hidden;
   const int z_off = L->conv_dim, a_off = L->conv_dim + L->vd, b_off = a_off + L->hv;
   GemmEpiArgs ep;
@@ -415,7 +456,19 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   ep.nheads = L->hv;
   ep.a_log = L->a_log;
   ep.dt_bias = L->dt_bias;
-  GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
+  uint8_t* xq = static_cast<uint8_t*>(q8);
+  float* xs = q8 ? reinterpret_cast<float*>(xq + align256(static_cast<size_t>(B) * h)) : nullptr;
+  uint8_t* yq = q8 ? reinterpret_cast<uint8_t*>(xs) + align256(static_cast<size_t>(B) * 4) : nullptr;
+  float* ys = q8 ? reinterpret_cast<float*>(yq + align256(static_cast<size_t>(B) * L->vd)) : nullptr;
+  if (q8) {
+    GDN_CUDA(quantize_rows_fp8(x, h, B, h, xq, xs, stream));
+    ep.a_tiled = L->w_in8;
+    ep.row_scale = L->s_in;
+    ep.col_scale = xs;
+    GDN_CUDA(gemm_f8_tn(L->w_in8, xq, h, L->rows, B, h, kEpiDecodeInProj, ep, stream, true, true));
+  } else {
+    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
+  }
   if (marks) {
     GDN_CUDA(stage_mark(L, 1, stream));
     GDN_CUDA(stage_mark(L, 2, stream));
@@ -448,7 +501,15 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   eo.a_tiled = L->w_out;
   eo.slot_epoch = slot_epoch;
   eo.slot_bytes = slot_bytes;
-  GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
+  if (q8) {
+    GDN_CUDA(quantize_rows_fp8(y, L->vd, B, L->vd, yq, ys, stream));
+    eo.a_tiled = L->w_out8;
+    eo.row_scale = L->s_out;
+    eo.col_scale = ys;
+    GDN_CUDA(gemm_f8_tn(L->w_out8, yq, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true));
+  } else {
+    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
+  }
   if (marks) GDN_CUDA(stage_mark(L, 5, stream));
   return GDN_OK;
 }
@@ -467,11 +528,12 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const int64_t n = static_cast<int64_t>(B) * T;
   const int64_t chunks = T > 1 ? static_cast<int64_t>(B) * ((T + 63) / 64) : 0;
-  gdn_status st = ensure_workspace(L, n, chunks, stream);
+  const bool f8 = T == 1 && L->w_in8;
+  gdn_status st = ensure_workspace(L, n, chunks, stream, f8);
   if (st != GDN_OK) return st;
   const int h = L->dims.hidden;
   char* ws = static_cast<char*>(L->ws->ptr);
-  const WsLayout lay = ws_layout(L, n, chunks);
+  const WsLayout lay = ws_layout(L, n, chunks, f8);
   float* proj = reinterpret_cast<float*>(ws);
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + lay.y);
   float* conv_tail = reinterpret_cast<float*>(ws + lay.tail);
@@ -490,8 +552,9 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
     gdn_status ds =
         p2p ? decode_chain(L, x, B, rec_state, conv_state, proj, y,
                            reinterpret_cast<uint16_t*>(comm->sym + kP2PSlotOffset), stream, true, p2p_epoch,
-                           static_cast<int64_t>(kP2PSlotBytes))
-            : decode_chain(L, x, B, rec_state, conv_state, proj, y, out, stream, true);
+                           static_cast<int64_t>(kP2PSlotBytes), f8 ? ws + lay.q8 : nullptr)
+            : decode_chain(L, x, B, rec_state, conv_state, proj, y, out, stream, true, nullptr, 0,
+                           f8 ? ws + lay.q8 : nullptr);
     if (ds != GDN_OK) return ds;
   } else {
     // ---- prefill: in_proj with the causal conv + SiLU fused into its epilogue -> conv-state roll ->
@@ -589,6 +652,8 @@ extern "C" gdn_status gdn_layer_decode_static(gdn_layer* L, const uint16_t* x, i
   if (!L || !x || !rec_state || !conv_state || !out)
     return fail(GDN_ERR_NULL_POINTER, "gdn_layer_decode_static: null argument");
   if (B <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_layer_decode_static: batch %d must be > 0", B);
+  if (L->w_in8)
+    return fail(GDN_ERR_UNSUPPORTED, "gdn_layer_decode_static: not available for fp8 weights (use gdn_layer_forward)");
   if (!aligned16(x) || !aligned16(out) || !aligned16(rec_state) || !aligned16(conv_state))
     return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_layer_decode_static: tensors must be 16-byte aligned");
   const size_t proj_bytes = align256(static_cast<size_t>(B) * L->proj_ld * 4);

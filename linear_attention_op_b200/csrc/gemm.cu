@@ -13,6 +13,8 @@
 //            causal conv, the conv-state roll and the gating scalars into the epilogue;
 //   out_proj (9B/gdn_layer.py:272-276).
 #include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -112,12 +114,24 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
   }
 }
 
-template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, int ksplit, int n_tiles, int group_m, int trigger_early, const uint8_t* a_tiled,
-                   const uint8_t* b_tiled, GemmEpiArgs ep) {
+// Row and column scales of the fp8 operands (per weight row, per activation row), applied before the
+// epilogue proper.
+__device__ __forceinline__ void apply_scales(const GemmEpiArgs& ep, int m, int n0, int M, int N, float (&v)[16]) {
+  if (!ep.row_scale || m >= M) return;
+  const float rs = ep.row_scale[m];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] *= rs * (n0 + j < N ? ep.col_scale[n0 + j] : 0.f);
+}
+
+// One CTA of the tcgen05 GEMM.  F8: A and B are fp8 e4m3 (kind::f8f6f4, 32-deep MMAs) and a 128-byte
+// stage row holds 128 K elements instead of 64; everything else (stage bytes, swizzle, pipeline) is the
+// bf16 kernel's.
+template <int BN, int STAGES, int EPI, bool F8>
+__device__ __forceinline__ void gemm_tn_body(const CUtensorMap& tmA, const CUtensorMap& tmB, int M, int N, int K,
+                                             int ksplit, int n_tiles, int group_m, int trigger_early,
+                                             const uint8_t* a_tiled, const uint8_t* b_tiled, const GemmEpiArgs& ep) {
   using C = GemmCfg<BN, STAGES>;
+  constexpr int kBKe = F8 ? 2 * kBK : kBK;  // K elements per 128-byte stage row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -137,7 +151,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int gsize = min(m_tiles - first_m, group_m);
   const int m_tile = first_m + (tile % per_group) % gsize;
   const int n_tile = (tile % per_group) / gsize;
-  const int kblocks = (K + kBK - 1) / kBK;
+  const int kblocks = (K + kBKe - 1) / kBKe;
   const int kb0 = static_cast<int>(static_cast<int64_t>(split) * kblocks / ksplit);
   const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * kblocks / ksplit);
   const int nk = kb1 - kb0;
@@ -173,13 +187,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Operands stored pre-tiled (the layer's weights) arrive as contiguous 16 KB blocks, each already
       // in the 128B-swizzled shared-memory layout of a 128-row x 64 tile, by 1D bulk copies; the others
       // through their tensor maps.
-      const int kbt = (K + kBK - 1) / kBK;
+      const int kbt = kblocks;
       auto load_a = [&](int s, int kb) {
         if (a_tiled)
           bulk_load_hint(sA + s * C::kABytes, a_tiled + (static_cast<int64_t>(m_tile) * kbt + kb) * 16384, 16384,
                          &full[s], pol_a);
         else
-          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, m_tile * kBM, pol_a);
+          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBKe, m_tile * kBM, pol_a);
       };
       auto load_b = [&](int s, int kb) {
         if (b_tiled) {
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            b_tiled + (static_cast<int64_t>(n_tile * (BN / 128) + q) * kbt + kb) * 16384, 16384,
                            &full[s], pol_b);
         } else {
-          tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, n_tile * BN, pol_b);
+          tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBKe, n_tile * BN, pol_b);
         }
       };
       const int pre = nk < STAGES ? nk : STAGES;
@@ -214,7 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_dense(1, kBM, BN);
+      constexpr uint32_t idesc = idesc_dense(F8 ? 0 : 1, kBM, BN);  // e4m3 x e4m3, or bf16 x bf16
       for (int i = 0; i < nk; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1, kErrWaitTmaFull)) break;
@@ -222,8 +236,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint64_t da = sdesc_k_sw128(smem_u32(sA + s * C::kABytes));
         const uint64_t db = sdesc_k_sw128(smem_u32(sB + s * C::kBBytes));
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)  // +32 bytes along K inside the swizzle row = +2 in the descriptor
-          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA (16 bf16 or 32 fp8) = +2 in the descriptor
+          if constexpr (F8)
+            umma_f8(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          else
+            umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
@@ -250,6 +268,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(t_row + c0, v);
+        apply_scales(eo, m, n_tile * BN + c0, M, N, v);
         epilogue16<EPI>(eo, m, n_tile * BN + c0, M, N, v);
       }
     }
@@ -294,6 +313,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
+        apply_scales(eo, m, n_tile * BN + c0, M, N, v);
         epilogue16<EPI>(eo, m, n_tile * BN + c0, M, N, v);
       }
     }
@@ -303,6 +323,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, int ksplit, int n_tiles, int group_m, int trigger_early, const uint8_t* a_tiled,
+                   const uint8_t* b_tiled, GemmEpiArgs ep) {
+  gemm_tn_body<BN, STAGES, EPI, false>(tmA, tmB, M, N, K, ksplit, n_tiles, group_m, trigger_early, a_tiled, b_tiled,
+                                       ep);
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_f8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                      int N, int K, int ksplit, int n_tiles, int group_m, int trigger_early, const uint8_t* a_tiled,
+                      const uint8_t* b_tiled, GemmEpiArgs ep) {
+  gemm_tn_body<BN, STAGES, EPI, true>(tmA, tmB, M, N, K, ksplit, n_tiles, group_m, trigger_early, a_tiled, b_tiled,
+                                      ep);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -395,17 +433,20 @@ static int one_wave_ksplit(Kern kern, int smem, int tiles, int kmax, int (&cap)[
   return 1;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool F8 = false>
 static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit,
                                const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t stream) {
   using C = GemmCfg<BN, STAGES>;
-  auto kern = gemm_tn_kernel<BN, STAGES, EPI>;
+  auto kern = [] {
+    if constexpr (F8) return gemm_tn_f8_kernel<BN, STAGES, EPI>;
+    else return gemm_tn_kernel<BN, STAGES, EPI>;
+  }();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int m_tiles = (M + kBM - 1) / kBM;
   const int n_tiles = (N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
-  const int kblocks = (K + kBK - 1) / kBK;
+  const int kblocks = (K + (F8 ? 2 * kBK : kBK) - 1) / (F8 ? 2 * kBK : kBK);
   static int cap[9] = {0};  // clusters of each size this instantiation fits on the device, filled on first use
   if (ksplit == 0) ksplit = choose_ksplit(kern, C::kSmemBytes, tiles, kblocks, cap);
   if (ksplit < 0) ksplit = one_wave_ksplit(kern, C::kSmemBytes, tiles, std::min(-ksplit, kblocks), cap);
@@ -505,6 +546,212 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
     case 128: return dispatch_epi<128, 6>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
     default: return dispatch_epi<256, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// fp8 (e4m3) decode projections
+// ---------------------------------------------------------------------------------------------
+
+// Row-major e4m3 matrix [rows, cols] (one byte per element, row stride ld bytes), tiles of 128 (K) x
+// box_rows, 128B swizzle: the same shared-memory image per 128-byte row as the bf16 maps.
+static cudaError_t make_tmap_u8(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                                int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld & 15) || rows <= 0 || cols <= 0 || ld < cols)
+    return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(2 * kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int BN, int STAGES>
+static cudaError_t dispatch_epi_f8(int epi, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                                   int ksplit, const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t s) {
+  switch (epi) {
+    case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T, true>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiDecodeInProj:
+      return launch_gemm<BN, STAGES, kEpiDecodeInProj, true>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t gemm_f8_tn(const void* A_tiled, const void* B, int64_t ldb, int M, int N, int K, int epi,
+                       const GemmEpiArgs& ep, cudaStream_t stream, bool pdl, bool trigger) {
+  if (M <= 0 || N <= 0 || K <= 0 || (K % (2 * kBK)) || !A_tiled || ep.a_tiled != A_tiled || !ep.row_scale ||
+      !ep.col_scale || ep.b_tiled)
+    return cudaErrorInvalidValue;
+  const int BN = N <= 16 ? 16 : (N <= 32 ? 32 : 64);
+  CUtensorMap ta, tb;
+  std::memset(&ta, 0, sizeof(ta));
+  std::memset(&tb, 0, sizeof(tb));
+  cudaError_t e = make_tmap_u8(&tb, B, N, K, ldb, BN);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int k1 = sms / tiles;
+  const bool two_per_sm = k1 == 0;
+  const int ksplit = -std::max(1, std::min(8, two_per_sm ? 2 * sms / tiles : k1));  // < 0: one wave
+  if (two_per_sm) {
+    switch (BN) {
+      case 16: return dispatch_epi_f8<16, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+      case 32: return dispatch_epi_f8<32, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+      default: return dispatch_epi_f8<64, 4>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    }
+  }
+  switch (BN) {
+    case 16: return dispatch_epi_f8<16, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    case 32: return dispatch_epi_f8<32, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+    default: return dispatch_epi_f8<64, 8>(epi, ta, tb, M, N, K, ksplit, ep, pdl, trigger, stream);
+  }
+}
+
+// The smallest power of two 2^e with amax / 2^e <= 448 (e4m3's largest finite value), from the bits of
+// amax / 448: that value itself when it is a power of two, else the next power up; 1 for an all-zero row.
+__device__ __forceinline__ float e4m3_scale(float amax) {
+  if (!(amax > 0.f)) return 1.f;
+  const uint32_t b = __float_as_uint(__fdiv_rn(amax, 448.f));
+  const uint32_t ex = (b >> 23) & 0xffu;
+  if (ex == 0u) return __uint_as_float(1u << 23);  // below the normal range: 2^-126
+  return (b & 0x7fffffu) ? __uint_as_float((ex + 1u) << 23) : __uint_as_float(b);
+}
+
+// 8 floats (already divided by the scale, |v| <= 448) -> 8 e4m3 bytes (round to nearest even) and the
+// dequantised values v8 * scale as 8 bf16.
+__device__ __forceinline__ void e4m3_pack8(const float (&v)[8], float scale, uint2& q, uint4& deq) {
+  uint32_t qw[2];
+  uint32_t* dw = reinterpret_cast<uint32_t*>(&deq);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_fp8x2_storage_t p = __nv_cvt_float2_to_fp8x2(make_float2(v[2 * i], v[2 * i + 1]), __NV_SATFINITE, __NV_E4M3);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p, __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    const __nv_bfloat162 bb = __floats2bfloat162_rn(f.x * scale, f.y * scale);
+    dw[i] = *reinterpret_cast<const uint32_t*>(&bb);
+    if (i & 1) qw[i >> 1] |= static_cast<uint32_t>(p) << 16;
+    else qw[i >> 1] = static_cast<uint32_t>(p);
+  }
+  q = make_uint2(qw[0], qw[1]);
+}
+
+__device__ __forceinline__ float amax8_bf16(const uint4& v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  return m;
+}
+
+__device__ __forceinline__ void unpack8_bf16(const uint4& v, float inv, float (&o)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    o[2 * i] = f.x * inv;
+    o[2 * i + 1] = f.y * inv;
+  }
+}
+
+// One warp per (padded) weight row: lane l handles 16-byte chunk l % 8 of bf16 blocks kb = l / 8, + 4, ...
+__global__ void quantize_tiled_weights_kernel(uint8_t* __restrict__ w16, int rows, int cols, int prow_total,
+                                              uint8_t* __restrict__ w8, float* __restrict__ scale) {
+  const int row = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= prow_total) return;
+  const int mt = row / kBM, r = row % kBM, c = lane & 7;
+  const int kbt16 = cols / kBK, kbt8 = cols / (2 * kBK);
+  auto src = [&](int kb) {
+    return w16 + (static_cast<int64_t>(mt) * kbt16 + kb) * 16384 + r * 128 + ((c ^ (r & 7)) << 4);
+  };
+  float amax = 0.f;
+  for (int kb = lane >> 3; kb < kbt16; kb += 4) amax = fmaxf(amax, amax8_bf16(*reinterpret_cast<const uint4*>(src(kb))));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  const float s = e4m3_scale(amax), inv = 1.f / s;
+  if (lane == 0 && row < rows) scale[row] = s;
+  for (int kb = lane >> 3; kb < kbt16; kb += 4) {
+    uint4* p16 = reinterpret_cast<uint4*>(src(kb));
+    float v[8];
+    unpack8_bf16(*p16, inv, v);
+    uint2 q;
+    uint4 deq;
+    e4m3_pack8(v, s, q, deq);
+    *p16 = deq;
+    const int k0 = kb * kBK + c * 8, kb8 = k0 / (2 * kBK), b = k0 % (2 * kBK);
+    *reinterpret_cast<uint2*>(w8 + (static_cast<int64_t>(mt) * kbt8 + kb8) * 16384 + r * 128 +
+                              (((b >> 4) ^ (r & 7)) << 4) + (b & 15)) = q;
+  }
+}
+
+cudaError_t quantize_tiled_weights_fp8(void* w_tiled, int rows, int cols, void* w8, float* scale,
+                                       cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0 || (cols % (2 * kBK)) || !w_tiled || !w8 || !scale) return cudaErrorInvalidValue;
+  const int64_t prows = static_cast<int64_t>(tiled_weight_bytes(rows, cols) / 16384) / (cols / kBK) * kBM;
+  count_launch();
+  quantize_tiled_weights_kernel<<<static_cast<unsigned>((prows * 32 + 255) / 256), 256, 0, stream>>>(
+      static_cast<uint8_t*>(w_tiled), rows, cols, static_cast<int>(prows), static_cast<uint8_t*>(w8), scale);
+  return cudaGetLastError();
+}
+
+// One CTA per activation row.  Programmatic dependent launch: the next kernel may start at once (it waits
+// for this one before reading xq / xs); this one waits for the previous kernel before reading x.
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const uint16_t* __restrict__ x, int64_t ld, int cols,
+                                                            uint8_t* __restrict__ xq, float* __restrict__ xs) {
+  __shared__ float red[8];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * ld);
+  const int nc = cols / 8;
+  float amax = 0.f;
+  for (int i = tid; i < nc; i += 256) amax = fmaxf(amax, amax8_bf16(xr[i]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+  const float s = e4m3_scale(amax), inv = 1.f / s;
+  if (tid == 0) xs[row] = s;
+  uint2* q8 = reinterpret_cast<uint2*>(xq + static_cast<int64_t>(row) * cols);
+  for (int i = tid; i < nc; i += 256) {
+    float v[8];
+    unpack8_bf16(xr[i], inv, v);
+    uint2 q;
+    uint4 deq;
+    e4m3_pack8(v, s, q, deq);
+    q8[i] = q;
+  }
+}
+
+cudaError_t quantize_rows_fp8(const void* x, int64_t ld, int rows, int cols, void* xq, float* xs,
+                              cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0 || (cols % 16) || (ld % 8) || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(xq) & 15) || !xs)
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, quantize_rows_kernel, static_cast<const uint16_t*>(x), ld, cols,
+                            static_cast<uint8_t*>(xq), xs);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -43,6 +43,9 @@ struct GemmEpiArgs {
   // double-buffered slot of the NVLink all-reduce; the epoch is read after the previous kernel finished).
   const unsigned long long* slot_epoch = nullptr;
   int64_t slot_bytes = 0;
+  // gemm_f8_tn only: acc[m][n] is multiplied by row_scale[m] * col_scale[n] (the operands' e4m3 scales)
+  const float* row_scale = nullptr;
+  const float* col_scale = nullptr;
 };
 
 // A: [M, K] bf16 row-major with row stride lda (elements); B: [N, K] bf16 row-major with row stride ldb
@@ -76,6 +79,24 @@ cudaError_t make_tmap_plain(void* map, const void* ptr, int elem_bytes, int64_t 
 // an M-tile is one contiguous run of HBM.
 size_t tiled_weight_bytes(int rows, int cols);
 cudaError_t tile_weights_bf16(const void* src, int64_t ld, int rows, int cols, void* dst, cudaStream_t stream);
+
+// fp8 (e4m3) decode projections.  Every scale is a power of two (the smallest 2^e with max|row| / 2^e <=
+// 448), so e4m3 value * scale is exact in bf16 and fp32.
+//   quantize_tiled_weights_fp8: row-wise quantisation of a matrix pre-tiled by tile_weights_bf16 (rows x
+//     cols, cols % 128 == 0): w8 (tiled_weight_bytes(rows, cols) / 2 bytes) receives the e4m3 weights in the
+//     same streaming layout with 128-element K blocks, scale[rows] the scales, and the bf16 tiles are
+//     overwritten with the dequantised weights, so bf16 GEMMs over them use the same weights.
+//   quantize_rows_fp8: row-wise quantisation of bf16 activations x [rows, cols] (row stride ld) into
+//     xq [rows, cols] bytes and xs[rows]; launched with programmatic dependent launch.
+//   gemm_f8_tn: gemm_bf16_tn's weight-streaming path with A = w8 (pre-tiled e4m3, ep.a_tiled == A) and
+//     B = xq [N, K] (row stride ldb bytes), ep.row_scale / ep.col_scale set; epi kEpiStoreBF16T or
+//     kEpiDecodeInProj.
+cudaError_t quantize_tiled_weights_fp8(void* w_tiled, int rows, int cols, void* w8, float* scale,
+                                       cudaStream_t stream);
+cudaError_t quantize_rows_fp8(const void* x, int64_t ld, int rows, int cols, void* xq, float* xs,
+                              cudaStream_t stream);
+cudaError_t gemm_f8_tn(const void* A_tiled, const void* B, int64_t ldb, int M, int N, int K, int epi,
+                       const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false, bool trigger = false);
 
 // Number of kernel launches issued by this library since load (for the benchmark's launch count).
 uint64_t launch_count();

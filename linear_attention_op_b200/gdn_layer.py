@@ -24,6 +24,10 @@ from ._lib import Dims, LayerInfo, Weights, call
 HEAD_DIM = 128
 
 
+# The reference's weight_dtype (ttnn.bfloat16 / bfloat8_b) -> gdn_layer_set_weight_format's formats.
+WEIGHT_FORMATS = {"bf16": 0, "fp8": 1}
+
+
 def _stream_handle(stream: torch.cuda.Stream | None = None) -> ctypes.c_void_p:
     s = stream if stream is not None else torch.cuda.current_stream()
     return ctypes.c_void_p(s.cuda_stream)
@@ -151,20 +155,28 @@ class Qwen35GatedDeltaNet:
     (any device/dtype) returns ``[B, T, hidden]`` on x's device in x's dtype; T == 1 is a decode step,
     T > 1 a chunked prefill.  ``tp_rank``/``tp_size``/``comm`` shard the heads over GPUs (one NCCL
     all-reduce per call); with ``tp_size > 1`` and ``comm=None`` the call returns this rank's partial sum.
+    ``weight_dtype="fp8"`` (the reference's ``weight_dtype=ttnn.bfloat8_b`` mode) quantises the projection
+    weights to e4m3 with per-row power-of-two scales: decode steps stream half the weight bytes (their
+    activations are quantised per token the same way), prefill uses the dequantised weights.
     """
 
     def __init__(self, hf_layer=None, batch: int = 1, *, weights=None, device=None, tp_rank: int = 0,
-                 tp_size: int = 1, comm=None, max_rows: int | None = None):
+                 tp_size: int = 1, comm=None, max_rows: int | None = None, weight_dtype: str = "bf16"):
         if (hf_layer is None) == (weights is None):
             raise ValueError("pass exactly one of hf_layer or weights")
         if batch <= 0:
             raise ValueError("batch must be > 0")
+        if weight_dtype not in WEIGHT_FORMATS:
+            raise ValueError(f"weight_dtype must be one of {sorted(WEIGHT_FORMATS)}")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.batch = batch
         self.comm = comm
         w = LayerWeights.from_any(hf_layer if hf_layer is not None else weights)
         with torch.cuda.device(self.device):
             self._h = _LayerHandle(w, tp_rank, tp_size)
+            if weight_dtype != "bf16":  # before any reserve: fp8 decode calls need more workspace
+                call("gdn_layer_set_weight_format", self._h.handle, WEIGHT_FORMATS[weight_dtype])
+        self.weight_dtype = weight_dtype
         info = self._h.info
         self.hidden = info.hidden
         self.nk, self.nv = w.num_k_heads, w.num_v_heads
@@ -270,10 +282,10 @@ class GDNStack:
     shares its scratch buffers."""
 
     def __init__(self, hf_layers, batch: int = 1, *, device=None, tp_rank: int = 0, tp_size: int = 1, comm=None,
-                 max_rows: int | None = None):
+                 max_rows: int | None = None, weight_dtype: str = "bf16"):
         self.batch = batch
         self.layers = [Qwen35GatedDeltaNet(weights=LayerWeights.from_any(L), batch=batch, device=device,
-                                           tp_rank=tp_rank, tp_size=tp_size, comm=comm)
+                                           tp_rank=tp_rank, tp_size=tp_size, comm=comm, weight_dtype=weight_dtype)
                        for L in hf_layers]
         for L in self.layers[1:]:
             L.share_workspace(self.layers[0])

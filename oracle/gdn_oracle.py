@@ -253,21 +253,24 @@ class LayerTrace:
 
 
 def layer_forward(w: GDNWeights, x: torch.Tensor, rec_state=None, conv_state=None, mode: str = "recurrent",
-                  chunk: int = 64, trace: bool = False):
+                  chunk: int = 64, trace: bool = False, act_fp8: bool = False):
     """One GDN layer call that continues from (rec_state, conv_state), in fp32.
 
     x: [B, T, hidden].  mode "recurrent" runs the token-by-token rule, "chunk" the chunked form.
     Returns (out [B, T, hidden], new rec_state [B, Hv, dk, dv], new conv_state [B, K-1, conv_dim]
     [, LayerTrace]).  Same sequence of steps as HF ``Qwen3_5GatedDeltaNet.forward`` and the reference's
     ``Qwen35GatedDeltaNetTT._forward_rows`` (``9B/gdn_layer.py:244-280``).
+    act_fp8: the projections' inputs are quantised per token to e4m3 (quantize_rows_e4m3; the out_proj
+    input after rounding to bf16) -- the library's fp8 decode; pair it with fp8_weights(w).
     """
     x = x.float()
+    x_in = quantize_rows_e4m3(x) if act_fp8 else x
     B, T, _ = x.shape
     kd, vd, Hk, Hv = w.key_dim, w.value_dim, w.num_k_heads, w.num_v_heads
-    qkv_pre = x @ w.w_qkv.float().T
-    z = x @ w.w_z.float().T
-    a = x @ w.w_a.float().T
-    b = x @ w.w_b.float().T
+    qkv_pre = x_in @ w.w_qkv.float().T
+    z = x_in @ w.w_z.float().T
+    a = x_in @ w.w_a.float().T
+    b = x_in @ w.w_b.float().T
     qkv, new_conv = causal_conv1d(qkv_pre, w.conv_w, conv_state)
     q = qkv[..., :kd].reshape(B, T, Hk, w.head_k_dim)
     k = qkv[..., kd:2 * kd].reshape(B, T, Hk, w.head_k_dim)
@@ -280,7 +283,7 @@ def layer_forward(w: GDNWeights, x: torch.Tensor, rec_state=None, conv_state=Non
     else:
         raise ValueError(f"unknown mode {mode!r}")
     y = rmsnorm_gated(o, z.reshape(B, T, Hv, w.head_v_dim), w.norm_w, w.eps).reshape(B, T, vd)
-    out = y @ w.w_out.float().T
+    out = (quantize_rows_e4m3(bf16_round(y)) if act_fp8 else y) @ w.w_out.float().T
     if trace:
         return out, S, new_conv, LayerTrace(qkv_pre, z, g, beta, qkv, o, y)
     return out, S, new_conv
@@ -308,6 +311,42 @@ def abi_conv_state_to_hf(state: torch.Tensor, oldest: torch.Tensor | None = None
 
 def bf16_round(t: torch.Tensor) -> torch.Tensor:
     return t.to(torch.bfloat16).float()
+
+
+# ------------------------------------------------------------------------------------------------
+# fp8 (e4m3) weights and activations: the library's fp8 mode, the B200 counterpart of the reference's
+# block-float weight modes (weight_dtype=ttnn.bfloat8_b, 9B/gdn_layer.py:55,90-119; 0.8B/gdn_l1.py:155).
+# ------------------------------------------------------------------------------------------------
+
+
+def e4m3_scale(amax: torch.Tensor) -> torch.Tensor:
+    """Per-row scale: the smallest power of two 2^e with amax / 2^e <= 448 (e4m3's largest finite value),
+    read from the bits of the fp32 quotient amax / 448 (that value when it is a power of two, else the next
+    power up; 2^-126 below the normal range); 1 where amax is 0."""
+    v = (amax.float() / 448.0).contiguous()
+    bits = v.view(torch.int32)
+    ex = (bits >> 23) & 0xFF
+    up = torch.where((bits & 0x7FFFFF) != 0, (ex + 1) << 23, bits)
+    up = torch.where(ex == 0, torch.full_like(bits, 1 << 23), up)
+    s = up.view(torch.float32)
+    return torch.where(amax > 0, s, torch.ones_like(s))
+
+
+def quantize_rows_e4m3(t: torch.Tensor) -> torch.Tensor:
+    """Row-wise (last dim) e4m3 round trip with e4m3_scale: round-to-nearest-even e4m3 of t / scale, times
+    the scale (exact: the scale is a power of two)."""
+    t = t.float()
+    s = e4m3_scale(t.abs().amax(dim=-1))[..., None]
+    return (t / s).to(torch.float8_e4m3fn).float() * s
+
+
+def fp8_weights(w: GDNWeights) -> GDNWeights:
+    """The weights the library's fp8 mode computes with: every output row of the projections quantised by
+    quantize_rows_e4m3 (conv taps, gates and norm weight unchanged)."""
+    from dataclasses import replace
+
+    return replace(w, w_qkv=quantize_rows_e4m3(w.w_qkv), w_z=quantize_rows_e4m3(w.w_z),
+                   w_a=quantize_rows_e4m3(w.w_a), w_b=quantize_rows_e4m3(w.w_b), w_out=quantize_rows_e4m3(w.w_out))
 
 
 def make_weights(hidden: int, num_k_heads: int, num_v_heads: int, head_dim: int = 128, conv_k: int = 4,
