@@ -23,16 +23,21 @@ from __future__ import annotations
 
 import torch
 
-from .gdn_layer import LayerWeights, _LayerHandle
+from ._lib import call
+from .gdn_layer import WEIGHT_FORMATS, LayerWeights, _LayerHandle
 
 
 class _PatchedGDN:
-    def __init__(self, module, device):
+    def __init__(self, module, device, weight_dtype: str = "bf16"):
+        if weight_dtype not in WEIGHT_FORMATS:
+            raise ValueError(f"weight_dtype must be one of {sorted(WEIGHT_FORMATS)}")
         self.module = module
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.layer_idx = getattr(module, "layer_idx", 0)
         with torch.cuda.device(self.device):
             self.handle = _LayerHandle(LayerWeights.from_hf(module))
+            if weight_dtype != "bf16":
+                call("gdn_layer_set_weight_format", self.handle.handle, WEIGHT_FORMATS[weight_dtype])
         info = self.handle.info
         self.hv, self.conv_dim = info.num_v_heads_local, info.conv_dim_local
         self.hidden = info.hidden
@@ -68,18 +73,19 @@ class _PatchedGDN:
         return out.to(device=hidden_states.device, dtype=hidden_states.dtype)
 
 
-def patch_gated_deltanet(module, device=None):
-    """Make ``module`` (a HF ``Qwen3_5GatedDeltaNet``) run on the B200 library; returns the module."""
-    module._gdn_b200 = _PatchedGDN(module, device)
+def patch_gated_deltanet(module, device=None, weight_dtype: str = "bf16"):
+    """Make ``module`` (a HF ``Qwen3_5GatedDeltaNet``) run on the B200 library; returns the module.
+    weight_dtype "fp8": the library's e4m3 weight mode (see Qwen35GatedDeltaNet)."""
+    module._gdn_b200 = _PatchedGDN(module, device, weight_dtype)
     module.forward = module._gdn_b200
     return module
 
 
-def patch_model(model, device=None) -> int:
+def patch_model(model, device=None, weight_dtype: str = "bf16") -> int:
     """Patch every ``Qwen3_5GatedDeltaNet`` inside ``model``; returns how many were patched."""
     n = 0
     for m in model.modules():
         if type(m).__name__ == "Qwen3_5GatedDeltaNet" and not hasattr(m, "_gdn_b200"):
-            patch_gated_deltanet(m, device)
+            patch_gated_deltanet(m, device, weight_dtype)
             n += 1
     return n
