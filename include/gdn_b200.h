@@ -185,6 +185,12 @@ GDN_API gdn_status gdn_comm_destroy(gdn_comm* comm);
  * inside the kernels set; 0 = no error. */
 GDN_API gdn_status gdn_device_error(int32_t* code_out);
 
+/* Failure-detection self-test: one thread waits, with the all-reduce's bounded peer wait, until the u64 at
+ * the device address `flag` reaches `value`.  A flag that nothing sets makes the wait expire (after 2 s);
+ * the kernel then records GDN's peer-wait error code (0x105) in the device error word and returns, and the
+ * context stays usable.  Lets a test exercise the timeout path without a second rank or any GPU fault. */
+GDN_API gdn_status gdn_selftest_peer_wait(const uint64_t* flag, uint64_t value, void* stream);
+
 /* Human-readable description of the last error on the calling thread ("" if none). */
 GDN_API const char* gdn_last_error_string(void);
 

@@ -171,6 +171,17 @@ __global__ void __launch_bounds__(256) allreduce_p2p_kernel(P2PAllReduceArgs a) 
   }
 }
 
+__global__ void peer_wait_selftest_kernel(const unsigned long long* flag, unsigned long long value) {
+  wait_flag(flag, value);
+}
+
+cudaError_t peer_wait_selftest(const unsigned long long* flag, unsigned long long value, cudaStream_t stream) {
+  if (!flag || (reinterpret_cast<uintptr_t>(flag) & 7)) return cudaErrorInvalidValue;
+  count_launch();
+  peer_wait_selftest_kernel<<<1, 1, 0, stream>>>(flag, value);
+  return cudaGetLastError();
+}
+
 cudaError_t allreduce_p2p(const P2PAllReduceArgs& a, cudaStream_t stream) {
   if (a.world < 2 || a.world > kP2PMaxRanks || a.rank < 0 || a.rank >= a.world || a.n <= 0 || (a.n & 7) || !a.out)
     return cudaErrorInvalidValue;

@@ -777,6 +777,13 @@ extern "C" gdn_status gdn_device_error(int32_t* code_out) {
   return GDN_OK;
 }
 
+extern "C" gdn_status gdn_selftest_peer_wait(const uint64_t* flag, uint64_t value, void* stream) {
+  if (!flag) return fail(GDN_ERR_NULL_POINTER, "gdn_selftest_peer_wait: null flag");
+  GDN_CUDA(peer_wait_selftest(reinterpret_cast<const unsigned long long*>(flag), value,
+                              static_cast<cudaStream_t>(stream)));
+  return GDN_OK;
+}
+
 extern "C" const char* gdn_last_error_string(void) { return t_last_error.c_str(); }
 
 extern "C" uint64_t gdn_kernel_launch_count(void) { return launch_count(); }

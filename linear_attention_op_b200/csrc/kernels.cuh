@@ -101,5 +101,7 @@ struct P2PAllReduceArgs {
   int rank = 0, world = 1;
 };
 cudaError_t allreduce_p2p(const P2PAllReduceArgs& a, cudaStream_t stream);
+// One thread waits (bounded, as the all-reduce waits for a peer) until *flag >= value.
+cudaError_t peer_wait_selftest(const unsigned long long* flag, unsigned long long value, cudaStream_t stream);
 
 }  // namespace gdn
