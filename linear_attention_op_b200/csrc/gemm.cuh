@@ -39,7 +39,7 @@ struct GemmEpiArgs {
   // Operands stored pre-tiled by tile_weights_bf16 (then A / B must equal these pointers; lda / ldb unused).
   const void* a_tiled = nullptr;
   const void* b_tiled = nullptr;
-  // gemm_bf16_tn only: when set, the output goes to out + ((*slot_epoch + 1) % 2) * slot_bytes (the
+  // gemm_bf16_tn and gemm_f8_tn: when set, the output goes to out + ((*slot_epoch + 1) % 2) * slot_bytes (the
   // double-buffered slot of the NVLink all-reduce; the epoch is read after the previous kernel finished).
   const unsigned long long* slot_epoch = nullptr;
   int64_t slot_bytes = 0;
