@@ -399,13 +399,28 @@ extern "C" gdn_status gdn_layer_set_weight_format(gdn_layer* L, int32_t format) 
   const int h = L->dims.hidden;
   if (h % 128 || L->vd % 128)
     return fail(GDN_ERR_UNSUPPORTED, "fp8 weights need hidden and value width multiples of 128");
-  GDN_CUDA(cudaMalloc(&L->w_in8, tiled_weight_bytes(L->rows, h) / 2));
-  GDN_CUDA(cudaMalloc(&L->w_out8, tiled_weight_bytes(h, L->vd) / 2));
-  GDN_CUDA(cudaMalloc(&L->s_in, static_cast<size_t>(L->rows) * 4));
-  GDN_CUDA(cudaMalloc(&L->s_out, static_cast<size_t>(h) * 4));
-  GDN_CUDA(quantize_tiled_weights_fp8(L->w_in, L->rows, h, L->w_in8, L->s_in, nullptr));
-  GDN_CUDA(quantize_tiled_weights_fp8(L->w_out, h, L->vd, L->w_out8, L->s_out, nullptr));
-  GDN_CUDA(cudaDeviceSynchronize());
+  // The layer switches only once everything succeeded; before that a failure leaves it bf16.  (A failure
+  // after the first in-place quantisation would leave w_in dequantised: that is reported as a CUDA error.)
+  uint8_t *w_in8 = nullptr, *w_out8 = nullptr;
+  float *s_in = nullptr, *s_out = nullptr;
+  cudaError_t e = cudaMalloc(&w_in8, tiled_weight_bytes(L->rows, h) / 2);
+  if (e == cudaSuccess) e = cudaMalloc(&w_out8, tiled_weight_bytes(h, L->vd) / 2);
+  if (e == cudaSuccess) e = cudaMalloc(&s_in, static_cast<size_t>(L->rows) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s_out, static_cast<size_t>(h) * 4);
+  if (e == cudaSuccess) e = quantize_tiled_weights_fp8(L->w_in, L->rows, h, w_in8, s_in, nullptr);
+  if (e == cudaSuccess) e = quantize_tiled_weights_fp8(L->w_out, h, L->vd, w_out8, s_out, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    for (void* p : {static_cast<void*>(w_in8), static_cast<void*>(w_out8), static_cast<void*>(s_in),
+                    static_cast<void*>(s_out)})
+      if (p) cudaFree(p);
+    return fail(e == cudaErrorMemoryAllocation ? GDN_ERR_OUT_OF_MEMORY : GDN_ERR_CUDA,
+                "gdn_layer_set_weight_format: %s", cudaGetErrorString(e));
+  }
+  L->w_in8 = w_in8;
+  L->w_out8 = w_out8;
+  L->s_in = s_in;
+  L->s_out = s_out;
   return GDN_OK;
 }
 
