@@ -314,6 +314,53 @@ def bf16_round(t: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------------------------------------
+# The decoder layer around the mixer (linear-attention layer type): input RMSNorm, GDN mixer, residual,
+# post-mixer RMSNorm, SwiGLU MLP, residual -- HF transformers 5.5.0 ``Qwen3_5DecoderLayer.forward``,
+# ``Qwen3_5RMSNorm`` and ``Qwen3_5MLP`` (modeling_qwen3_5.py).  The reference stacks GDN mixers only
+# (0.8B/gdn_l1.py:295-325); its optimisation notes name these surroundings as the next step
+# (0.8B/OPTIMIZATION.md:258-259).
+# ------------------------------------------------------------------------------------------------
+
+
+@dataclass
+class DecoderWeights:
+    """One linear-attention decoder layer: the GDN mixer's weights plus its surroundings (fp32 tensors;
+    projections bf16-representable).  input_norm_w, post_norm_w [hidden] (applied as 1 + w);
+    w_gate, w_up [intermediate, hidden]; w_down [hidden, intermediate]."""
+
+    gdn: GDNWeights
+    input_norm_w: torch.Tensor
+    post_norm_w: torch.Tensor
+    w_gate: torch.Tensor
+    w_up: torch.Tensor
+    w_down: torch.Tensor
+    eps: float = 1e-6
+
+
+def rmsnorm_offset(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Qwen3_5RMSNorm: x * rsqrt(mean(x^2) + eps) * (1 + w), in fp32."""
+    x = x.float()
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + w.float())
+
+
+def swiglu_mlp(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """Qwen3_5MLP with hidden_act silu: down(silu(gate(x)) * up(x))."""
+    return (F.silu(x @ w_gate.float().T) * (x @ w_up.float().T)) @ w_down.float().T
+
+
+def decoder_layer_forward(dw: DecoderWeights, x: torch.Tensor, rec_state=None, conv_state=None,
+                          mode: str = "recurrent", chunk: int = 64):
+    """One decoder-layer call that continues from (rec_state, conv_state), in fp32; returns
+    (out [B, T, hidden], new rec_state, new conv_state)."""
+    x = x.float()
+    mixed, S, conv = layer_forward(dw.gdn, rmsnorm_offset(x, dw.input_norm_w, dw.eps), rec_state, conv_state,
+                                   mode=mode, chunk=chunk)
+    h = x + mixed
+    out = h + swiglu_mlp(rmsnorm_offset(h, dw.post_norm_w, dw.eps), dw.w_gate, dw.w_up, dw.w_down)
+    return out, S, conv
+
+
+# ------------------------------------------------------------------------------------------------
 # fp8 (e4m3) weights and activations: the library's fp8 mode, the B200 counterpart of the reference's
 # block-float weight modes (weight_dtype=ttnn.bfloat8_b, 9B/gdn_layer.py:55,90-119; 0.8B/gdn_l1.py:155).
 # ------------------------------------------------------------------------------------------------

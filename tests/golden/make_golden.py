@@ -13,7 +13,11 @@ Sources of truth (nothing here is re-implemented; every expected value comes fro
 * ``layer_hf.npz`` -- HF ``Qwen3_5GatedDeltaNet`` (torch fallback path, fp32) built the way
   ``9B/test_gdn_layer.py:19-28`` builds it (bf16-rounded projections, norm weight U(0.5, 1.5), dt_bias
   U(-1, 1)), at a small geometry with the Qwen3.5 head size (dk = dv = 128): a 2-sequence 40-token prefill
-  followed by 3 cached decode steps, plus a one-token call.
+  followed by 3 cached decode steps, plus a one-token call;
+* ``decoder_hf.npz`` -- HF ``Qwen3_5DecoderLayer`` of the linear-attention type (input RMSNorm, the GDN mixer,
+  residual, post-mixer RMSNorm, SwiGLU MLP, residual) at the same geometry with a 512-wide MLP: a 2-sequence
+  40-token prefill followed by 3 cached decode steps.  The reference stacks GDN mixers only; these are the
+  surroundings its optimisation notes name as the next step (0.8B/OPTIMIZATION.md:258-259).
 
 The fixtures are small (< 2 MB together) and committed; the GPU box never needs the reference checkout.
 """
@@ -117,16 +121,66 @@ def layer_case() -> dict:
     )
 
 
+def decoder_case() -> dict:
+    from transformers.cache_utils import DynamicCache
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5DecoderLayer
+
+    cfg = Qwen3_5TextConfig(hidden_size=256, linear_num_key_heads=2, linear_num_value_heads=4,
+                            linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4,
+                            rms_norm_eps=1e-6, num_hidden_layers=1, intermediate_size=512)
+    assert cfg.layer_types == ["linear_attention"] and cfg.hidden_act == "silu"
+    torch.manual_seed(2)
+    D = Qwen3_5DecoderLayer(cfg, layer_idx=0).eval()
+    L = D.linear_attn
+    with torch.no_grad():
+        L.norm.weight.uniform_(0.5, 1.5)
+        L.dt_bias.uniform_(-1.0, 1.0)
+        D.input_layernorm.weight.uniform_(-0.5, 0.5)  # applied as (1 + w)
+        D.post_attention_layernorm.weight.uniform_(-0.5, 0.5)
+        for lin in (L.in_proj_qkv, L.in_proj_z, L.in_proj_a, L.in_proj_b, L.out_proj, D.mlp.gate_proj,
+                    D.mlp.up_proj, D.mlp.down_proj):
+            lin.weight.copy_(lin.weight.bfloat16().float())
+        L.conv1d.weight.copy_(L.conv1d.weight.bfloat16().float())
+    gen = torch.Generator().manual_seed(3)
+    B, T0, steps = 2, 40, 3
+    x = torch.randn(B, T0 + steps, 256, generator=gen).bfloat16().float()
+    with torch.no_grad():
+        cache = DynamicCache(config=cfg)
+        y_pre = D(x[:, :T0], position_embeddings=None, past_key_values=cache)
+        y_dec = [D(x[:, t:t + 1], position_embeddings=None, past_key_values=cache) for t in range(T0, T0 + steps)]
+        conv_dec = cache.layers[0].conv_states.clone()
+        rec_dec = cache.layers[0].recurrent_states.clone()
+    bf = lambda t: t.detach().to(torch.bfloat16).view(torch.int16).numpy()
+    return dict(
+        w_qkv=bf(L.in_proj_qkv.weight), w_z=bf(L.in_proj_z.weight), w_a=bf(L.in_proj_a.weight),
+        w_b=bf(L.in_proj_b.weight), w_out=bf(L.out_proj.weight), conv_w=f32(L.conv1d.weight[:, 0, :]),
+        a_log=f32(L.A_log), dt_bias=f32(L.dt_bias), norm_w=f32(L.norm.weight),
+        dims=np.array([256, 2, 4, 128, 128, 4], np.int32),
+        input_norm_w=f32(D.input_layernorm.weight), post_norm_w=f32(D.post_attention_layernorm.weight),
+        w_gate=bf(D.mlp.gate_proj.weight), w_up=bf(D.mlp.up_proj.weight), w_down=bf(D.mlp.down_proj.weight),
+        x=f32(x), y_pre=f32(y_pre), y_dec=f32(torch.cat(y_dec, 1)), conv_dec=f32(conv_dec),
+        rec_dec=f32(rec_dec), t0=np.array([T0], np.int32),
+    )
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-dir", required=True,
                     help="the reference checkout's wormhole_n150/qwen3.5_9B directory (holds reference.py)")
+    ap.add_argument("--only", choices=["recurrence", "chunk", "layer", "decoder"], default=None,
+                    help="regenerate one fixture only (the others keep their committed bytes)")
     args = ap.parse_args(argv)
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = load_reference_module(args.reference_dir)
-    np.savez_compressed(HERE / "recurrence_ref.npz", **recurrence_cases(ref))
-    np.savez_compressed(HERE / "chunk_hf.npz", **chunk_case())
-    np.savez_compressed(HERE / "layer_hf.npz", **layer_case())
+    if args.only in (None, "recurrence"):
+        np.savez_compressed(HERE / "recurrence_ref.npz", **recurrence_cases(ref))
+    if args.only in (None, "chunk"):
+        np.savez_compressed(HERE / "chunk_hf.npz", **chunk_case())
+    if args.only in (None, "layer"):
+        np.savez_compressed(HERE / "layer_hf.npz", **layer_case())
+    if args.only in (None, "decoder"):
+        np.savez_compressed(HERE / "decoder_hf.npz", **decoder_case())
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -92,3 +92,23 @@ def test_short_call_keeps_older_conv_history():
     _, s1 = O.causal_conv1d(x[:, :4], w, None)
     _, s2 = O.causal_conv1d(x[:, 4:5], w, s1)
     assert torch.allclose(s_all, s2)
+
+
+@pytest.mark.parametrize("mode", ["recurrent", "chunk"])
+def test_decoder_layer_prefill_then_decode_matches_hf(golden_dir, mode):
+    """The decoder layer around the mixer (input RMSNorm, residual, SwiGLU MLP) against HF's
+    Qwen3_5DecoderLayer of the linear-attention type, prefill then cached decode."""
+    z = np.load(golden_dir / "decoder_hf.npz")
+    dw = O.DecoderWeights(gdn=layer_weights(z), input_norm_w=T(z["input_norm_w"]), post_norm_w=T(z["post_norm_w"]),
+                          w_gate=bf16(z["w_gate"]), w_up=bf16(z["w_up"]), w_down=bf16(z["w_down"]))
+    x = T(z["x"])
+    t0 = int(z["t0"][0])
+    y, s, c = O.decoder_layer_forward(dw, x[:, :t0], mode=mode)
+    assert O.max_abs_rel(y, T(z["y_pre"])) < 1e-4
+    ys = []
+    for t in range(t0, x.shape[1]):
+        yt, s, c = O.decoder_layer_forward(dw, x[:, t:t + 1], s, c, mode=mode)
+        ys.append(yt)
+    assert O.max_abs_rel(torch.cat(ys, 1), T(z["y_dec"])) < 1e-4
+    assert O.max_abs_rel(s, T(z["rec_dec"])) < 1e-4
+    assert O.max_abs_rel(c, O.hf_conv_state_to_abi(T(z["conv_dec"]))) < 1e-6
