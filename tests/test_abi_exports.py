@@ -102,3 +102,14 @@ def test_python_errors_raise():
     h = ctypes.c_void_p()
     with pytest.raises(GDNError, match="UNSUPPORTED"):
         call("gdn_layer_create", ctypes.byref(_dims(head_k_dim=64)), ctypes.byref(w), 0, 1, ctypes.byref(h))
+
+
+def test_workspace_format_and_selftest_entry_points_check_pointers():
+    """The workspace, weight-format and self-test entry points reject null handles before any CUDA call."""
+    lib = _lib.lib()
+    assert lib.gdn_layer_share_workspace(None, None) == 2
+    assert lib.gdn_layer_set_weight_format(None, 1) == 2
+    assert lib.gdn_layer_reserve(None, 64) == 2
+    assert lib.gdn_selftest_peer_wait(None, 1, None) == 2
+    assert lib.gdn_layer_decode_static(None, None, 1, None, None, None, None) == 2
+    assert lib.gdn_last_error_string()
