@@ -130,7 +130,8 @@ GDN_API gdn_status gdn_layer_set_weight_format(gdn_layer* layer, int32_t format)
 /* One layer call that continues from (rec_state, conv_state) and updates both in place:
  *   T == 1  decode step (one token per sequence);  T > 1  chunked prefill of T tokens per sequence.
  * out receives the layer output (bf16 [B, T, hidden]); with tp_size > 1 every rank receives the full,
- * all-reduced output (one NCCL all-reduce per call over `comm`).  With comm == NULL the call skips the
+ * all-reduced output (one all-reduce per call over `comm`: the NVLink peer-memory kernel for decode outputs
+ * up to 8 MiB, NCCL above).  With comm == NULL the call skips the
  * all-reduce and out holds this rank's partial sum (for callers that reduce themselves).
  * Replaces Qwen35GatedDeltaNetTT.__call__ / _forward_rows (9B/gdn_layer.py:244-292) and
  * Qwen35_08B_GDNStackL1.forward_device (0.8B/gdn_l1.py:295-307).  x may alias nothing else. */
