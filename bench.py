@@ -49,10 +49,34 @@ def peaks():
     return dict(FALLBACK_PEAKS, source="fallback")
 
 
-def ncu_traffic():
-    """Per-launch DRAM bytes of each kernel from the committed ncu summaries (profiles/ncu_traffic.json)."""
+def ncu_traffic(key: str, geometry: str):
+    """Per-launch DRAM bytes of one kernel from the committed ncu summary (profiles/ncu_traffic.json), or None
+    when that capture was made on another geometry (shard or batch) than the one being reported."""
     p = ROOT / "profiles" / "ncu_traffic.json"
-    return json.loads(p.read_text()) if p.exists() else {}
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(key) if d.get("_geometry", {}).get(key.split("_")[0]) == geometry else None
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def workload_config(world: int) -> dict:
+    """The benchmark configuration, the same dict in both arms (ours and --impl reference)."""
+    B = DECODE_B * world
+    return {"workload": f"cfg2: Qwen3.5-9B GDN layer decode, batch {DECODE_B} per GPU (global {B}), "
+                        "fp32 state ~N(0,0.1)",
+            "model": "Qwen3.5-9B GDN layer (random init)", "global_batch": B, "seq_len": 1,
+            "parallelism": f"tp{world} head-parallel" if world > 1 else "tp1",
+            "l2": "inputs larger than L2: 417 MB of weights + state per GPU per step > 126 MB"}
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -86,8 +110,9 @@ def decode_bytes(B: int, world: int = 1, wbytes: int = 2) -> dict:
     act = 2 * B * H * 2
     proj = B * rows * 4
     return {
-        "in_proj": w_in + B * H * 2 + conv + proj,
-        "recurrence": state + B * (2 * kd + 2 * vd + 2 * hv) * 4 + B * vd * 2,
+        # in_proj writes the raw fp32 projections; the conv (history read, state roll) runs in the step kernel
+        "in_proj": w_in + B * H * 2 + proj,
+        "recurrence": state + conv + proj + B * vd * 2,
         "out_proj": w_out + B * vd * 2 + B * H * 2,
         "step": w_in + w_out + state + conv + act,
     }
@@ -232,6 +257,78 @@ def stage_times(layer, run_step, steps: int) -> list[float]:
     return [t / steps for t in tot]
 
 
+def max_abs_rel(got: torch.Tensor, want: torch.Tensor) -> float:
+    """max|got - want| / max|want| (the benchmark spec's tolerance metric)."""
+    got, want = got.double(), want.double()
+    return float((got - want).abs().max() / want.abs().max().clamp_min(1e-30))
+
+
+def tp_parity(layer, W, rank: int, world: int, dev) -> dict:
+    """Multi-GPU correctness, checked before the timed region: the head-parallel layer (this rank's shard and
+    the library communicator) against a single-GPU layer (tp_size 1, the path the GPU test suite pins to the
+    CPU oracle) built from the same weights on this rank's GPU, on the same inputs.
+    * decode: one step at the benchmark's global batch from a random N(0, 0.1) state -- the NVLink
+      all-reduce at the timed message size;
+    * prefill: 2 sequences x 130 tokens from zero state -- the NCCL all-reduce, ragged last chunk.
+    Every rank compares its all-reduced output and its state shards; the worst error over the ranks is
+    reported, plus whether every rank received bit-identical outputs."""
+    import torch.distributed as dist
+
+    from linear_attention_op_b200 import Qwen35GatedDeltaNet
+
+    hv, kd, vd = HV // world, HK * D // world, HV * D // world
+    k0, v0 = rank * kd, rank * vd
+    conv_idx = torch.cat([torch.arange(k0, k0 + kd), HK * D + torch.arange(k0, k0 + kd),
+                          2 * HK * D + torch.arange(v0, v0 + vd)]).to(dev)
+    B = layer.batch
+    ref = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev)
+    g = torch.Generator(device=dev).manual_seed(77)  # identical on every rank
+    s0 = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.1
+    c0 = torch.randn(B, 3, 2 * HK * D + HV * D, generator=g, device=dev)
+    x = torch.randn(B, 1, H, generator=g, device=dev).to(torch.bfloat16)
+    xp = torch.randn(2, 130, H, generator=g, device=dev).to(torch.bfloat16)
+    res = {}
+    tp = layer.with_batch(B)
+    tp.set_state(rec_state=s0[:, rank * hv:(rank + 1) * hv], conv_state=c0[:, :, conv_idx])
+    ref.set_state(rec_state=s0, conv_state=c0)
+    out_tp = tp.forward_into(x, torch.empty_like(x))
+    out_ref = ref.forward_into(x, torch.empty_like(x))
+    torch.cuda.synchronize()
+    res["decode_out"] = max_abs_rel(out_tp.float(), out_ref.float())
+    res["decode_state"] = max_abs_rel(tp.rec_state, ref.rec_state[:, rank * hv:(rank + 1) * hv])
+    res["decode_conv_state"] = max_abs_rel(tp.conv_state, ref.conv_state[:, :, conv_idx])
+    sums = [out_tp.float().sum().double()]
+    del tp, s0
+    tp2, ref2 = layer.with_batch(2), ref.with_batch(2)
+    outp_tp = tp2.forward_into(xp, torch.empty_like(xp))
+    outp_ref = ref2.forward_into(xp, torch.empty_like(xp))
+    torch.cuda.synchronize()
+    res["prefill_out"] = max_abs_rel(outp_tp.float(), outp_ref.float())
+    res["prefill_state"] = max_abs_rel(tp2.rec_state, ref2.rec_state[:, rank * hv:(rank + 1) * hv])
+    res["prefill_conv_state"] = max_abs_rel(tp2.conv_state, ref2.conv_state[:, :, conv_idx])
+    sums.append(outp_tp.float().sum().double())
+    del tp2, ref2, ref
+    t = torch.tensor([res[k] for k in sorted(res)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    res = {k: float(v) for k, v in zip(sorted(res), t.tolist())}
+    cs = torch.stack(sums).to(dev)
+    allcs = [torch.empty_like(cs) for _ in range(world)]
+    dist.all_gather(allcs, cs)
+    res["ranks_identical"] = all(torch.equal(allcs[0], c) for c in allcs)
+    res["tolerance"] = {"out": 2e-2, "state": 1e-3, "conv_state": 1e-4}
+    res["ok"] = bool(res["ranks_identical"] and res["decode_out"] <= 2e-2 and res["prefill_out"] <= 2e-2
+                     and res["decode_state"] <= 1e-3 and res["prefill_state"] <= 1e-3
+                     and res["decode_conv_state"] <= 1e-4 and res["prefill_conv_state"] <= 1e-4)
+    res["against"] = "single-GPU layer (tp1) with the same weights and inputs on each rank's GPU"
+    return res
+
+
+def graph_steps_for(steps: int, want: int) -> int:
+    """The largest divisor of `steps` not above `want`: every replay holds the same number of steps and the
+    timed region holds exactly `steps` of them."""
+    return max(d for d in range(1, max(1, min(want, steps)) + 1) if steps % d == 0)
+
+
 def run_ours(args):
     from linear_attention_op_b200 import Qwen35GatedDeltaNet, device_error, launch_count
     from linear_attention_op_b200.tp import Communicator
@@ -239,7 +336,6 @@ def run_ours(args):
     rank, world, local = setup_dist(args.gpus)
     dev = torch.device("cuda", local)
     pk = peaks()
-    traffic = ncu_traffic()
     comm = Communicator.from_process_group() if world > 1 else None
     W = synthetic_weights(0, dev)
     B = DECODE_B * world  # 64 sequences per GPU: each GPU holds all of them for its 1/N of the heads
@@ -247,12 +343,13 @@ def run_ours(args):
                                 max_rows=max(B, PREFILL_B * PREFILL_T if args.prefill else B),
                                 weight_dtype=args.weights)
     if args.only == "prefill":  # profiling case: the prefill workload alone
-        res = run_prefill(args, layer, dev, world, pk, traffic)
+        res = run_prefill(args, layer, dev, world, pk)
         if rank == 0:
             print(json.dumps({"metric": METRIC, "only": "prefill", "prefill": res}), flush=True)
         if comm is not None:
             comm.close()
         return
+    parity = tp_parity(layer, W, rank, world, dev) if world > 1 and args.weights == "bf16" else None
     g = torch.Generator(device=dev).manual_seed(1000 + rank)  # this rank's heads of the N(0, 0.1) state
     layer.set_state(rec_state=torch.randn(B, HV // world, D, D, generator=g, device=dev) * 0.1)
     gx = torch.Generator(device=dev).manual_seed(1)  # the replicated input, identical on every rank
@@ -272,7 +369,7 @@ def run_ours(args):
 
     # G consecutive decode steps per graph (as a model's graph holds many layers per token), so that the
     # host's graph launches do not pace the GPU; K timed steps = K / G replays.
-    gsteps = args.graph_steps if args.steps % args.graph_steps == 0 else 1
+    gsteps = graph_steps_for(args.steps, args.graph_steps)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(gsteps):
@@ -305,56 +402,63 @@ def run_ours(args):
     def dec_step():
         layer.forward_into(x, out, stream=torch.cuda.current_stream())
 
-    st = stage_times(layer, dec_step, min(args.steps, 50))
+    st = stage_times(layer, dec_step, min(max(args.steps, 20), 50))
     names = STAGES
     byt = decode_bytes(B, world, 1 if args.weights == "fp8" else 2)
     dec_stage = {n: round(t * 1e3, 2) for n, t in zip(names, st) if n not in ("conv", "chunk_prep")}
     dom = max(["in_proj", "recurrence", "out_proj"], key=lambda n: dec_stage[n])
     achieved = byt[dom] / (dec_stage[dom] * 1e-6) / 1e9
-    tr = traffic.get(f"decode_{dom}")
+    geom = f"9B B={B} tp{world} {args.weights}"
     roofline = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                "traffic": tr, "algorithmic_bytes": byt[dom], "peak_source": pk["source"]}
+                "traffic": ncu_traffic(f"decode_{dom}", geom), "algorithmic_bytes": byt[dom],
+                "peak_source": pk["source"] + " (HBM copy)"}
     step_achieved = byt["step"] / (ms_step * 1e-3) / 1e9
     decode_detail = {"stage_us": dec_stage, "step_bytes": byt["step"], "step_gbs": round(step_achieved, 1),
-                     "step_hbm_frac": round(step_achieved / pk["hbm_gbs"], 4)}
+                     "step_hbm_frac": round(step_achieved / pk["hbm_gbs"], 4),
+                     "graph": f"{gsteps} consecutive decode steps per CUDA-graph replay"}
 
-    # end to end through the public API, host buffers (pinned), H2D + D2H inside the timed region
+    # End to end through the public API with pinned host buffers: every step copies its input host->device
+    # and its result device->host inside the timed region (forward_host_async: the copies run on copy streams
+    # with double-buffered device rows, overlapping the neighbouring steps' compute).
     xh = x.detach().cpu().pin_memory()
-    for _ in range(3):
-        layer(xh)
+    yh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
+    for i in range(3):
+        layer.forward_host_async(xh, yh[i % 2])
     torch.cuda.synchronize()
     barrier(world)
-    e2e_steps = min(args.steps, 100)
-    t0 = time.perf_counter()
+    e2e_steps = max(args.steps, 20)
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
     es.record()
-    for _ in range(e2e_steps):
-        yh = layer(xh)
+    for i in range(e2e_steps):
+        ev = layer.forward_host_async(xh, yh[i % 2])
+    ev.synchronize()
     ee.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(max(es.elapsed_time(ee), (time.perf_counter() - t0) * 1e3), world)
     e2e = {"value": round(B * e2e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-           "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": yh.numel() * yh.element_size(),
-           "steps": e2e_steps, "path": "Qwen35GatedDeltaNet.__call__ (C-ABI gdn_layer_forward)"}
+           "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+           "d2h_bytes_per_step": yh[0].numel() * yh[0].element_size(), "steps": e2e_steps,
+           "path": "Qwen35GatedDeltaNet.forward_host_async (C-ABI gdn_layer_forward), pinned host in/out, "
+                   "copies on copy streams overlapping the neighbouring steps",
+           "timing": "max of host wall clock and CUDA events around all steps, max over ranks"}
 
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": ("bf16 (fp32 state, fp32 accumulation)" if args.weights == "bf16" else
                   "fp8 e4m3 projection weights and decode activations, bf16 elsewhere (fp32 state, fp32 accumulation)"), "data": "synthetic",
-        "config": {"workload": f"cfg2: Qwen3.5-9B GDN layer decode, batch {DECODE_B} per GPU (global {B}), "
-                               "fp32 state ~N(0,0.1)",
-                   "model": "Qwen3.5-9B GDN layer (random init)", "global_batch": B, "seq_len": 1,
-                   "parallelism": f"tp{world} head-parallel" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2: 417 MB of weights + state per step > 126 MB",
-                   "graph": f"{gsteps} consecutive decode steps per CUDA-graph replay"},
+        "config": workload_config(world),
         "roofline": roofline, "decode": decode_detail, "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step,
         "clocks": clk.summary(),
     }
+    if parity is not None:
+        result["parity"] = parity
     if args.prefill:
-        result["prefill"] = run_prefill(args, layer, dev, world, pk, traffic)
+        result["prefill"] = run_prefill(args, layer, dev, world, pk)
     if device_error() != 0:
         raise SystemExit("device error during the benchmark")
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -368,9 +472,11 @@ def run_ours(args):
         import torch.distributed as dist
 
         dist.destroy_process_group()
+    if parity is not None and not parity["ok"]:
+        raise SystemExit(f"tensor-parallel parity failed: {parity}")
 
 
-def run_prefill(args, layer_dec, dev, world, pk, traffic):
+def run_prefill(args, layer_dec, dev, world, pk):
     """Config 3: batch 8 x 8192-token chunked prefill (weights shared with the decode layer)."""
     B, T = PREFILL_B, PREFILL_T
     layer_p = layer_dec.with_batch(B)  # same device weights, own batch and state
@@ -378,7 +484,7 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
     x = torch.randn(B, T, H, generator=g, device=dev).to(torch.bfloat16)
     out = torch.empty_like(x)
     steps = max(1, min(args.steps, args.prefill_steps))
-    for _ in range(2):
+    for _ in range(3):
         layer_p.forward_into(x, out)
     torch.cuda.synchronize()
     sampler = ClockSampler([dev.index] if int(os.environ.get("RANK", 0)) == 0 else None, 0.05 if world == 1 else None)
@@ -400,16 +506,18 @@ def run_prefill(args, layer_dec, dev, world, pk, traffic):
     fl = prefill_flops(B, T, world)
     tf = lambda n: fl[n] / (stage[n] * 1e-3) / 1e12
     rec_ms = stage["chunk_prep"] + stage["recurrence"]
+    peak = pk["bf16_tflops"]  # burst: a ~10 ms kernel in a region well under a second
+    geom = f"9B B={B} T={T} tp{world} {args.weights}"
     return {
         "workload": "cfg3: Qwen3.5-9B GDN layer chunked prefill, batch 8 x 8192 tokens, chunk 64",
         "value": round(B * T / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3), "steps": steps,
-        "stage_ms": stage,
+        "scaling": "strong", "stage_ms": stage,
         "roofline": {"kernel": "in_proj", "bound": "tensor", "achieved": round(tf("in_proj"), 1),
-                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                     "frac": round(tf("in_proj") / pk["bf16_tflops_sustained"], 4),
-                     "traffic": traffic.get("prefill_in_proj"), "peak_source": pk["source"] + " (sustained)"},
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(tf("in_proj") / peak, 4),
+                     "traffic": ncu_traffic("prefill_in_proj", geom), "algorithmic_flops": fl["in_proj"],
+                     "peak_source": pk["source"] + " (burst bf16)"},
         "step_tflops": round(fl["step"] / (ms * 1e-3) / 1e12, 1),
-        "step_tensor_frac": round(fl["step"] / (ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
+        "step_tensor_frac": round(fl["step"] / (ms * 1e-3) / 1e12 / peak, 4),
         "recurrence_tflops": round(fl["recurrence"] / (rec_ms * 1e-3) / 1e12, 2),
         "clocks": clk.summary(),
     }
@@ -442,7 +550,7 @@ def cpu_decode_rate(budget_s: float = 15.0, max_steps: int | None = None, warmup
 
 def cpu_baseline():
     rate, n, el, cores = cpu_decode_rate()
-    return {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+    return {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
             "sample": f"{n} cfg2 decode steps (batch 64, 9B GDN layer, fp32) in {el:.1f} s on the host cores"}
 
 
@@ -457,12 +565,12 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(rate, 1), "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": n, "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "cfg2: Qwen3.5-9B GDN layer decode, batch 64, fp32 state ~N(0,0.1)",
-                   "model": "Qwen3.5-9B GDN layer (random init)", "global_batch": DECODE_B, "seq_len": 1,
-                   "parallelism": "host CPU"},
+        "config": workload_config(args.gpus),
         "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} full cfg2 decode steps on the host cores (the reference's device code "
-                                   f"is Tenstorrent-only; this is its CPU golden path restated)"},
+                         "cpu": cpu_model(),
+                         "sample": f"{n} cfg2 decode steps of batch 64 on the host cores, each a bounded sample "
+                                   f"of the workload's {DECODE_B * args.gpus} sequences (the reference's device "
+                                   f"code is Tenstorrent-only; this is its CPU golden path restated)"},
         "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

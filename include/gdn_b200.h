@@ -100,9 +100,24 @@ GDN_API gdn_status gdn_layer_destroy(gdn_layer* layer);
 
 GDN_API gdn_status gdn_layer_get_info(const gdn_layer* layer, gdn_layer_info* info);
 
-/* Pre-allocate the workspace for calls of up to `max_tokens` = B*T rows, so that later forwards
- * allocate nothing (required before capturing forwards into a CUDA graph). */
+/* Pre-allocate the workspace for calls of up to `max_tokens` = B*T rows in at most 64 sequences, so that
+ * later forwards allocate nothing (required before capturing forwards into a CUDA graph).  The reference
+ * sizes its device buffers for max_rows rows in its constructor (9B/gdn_layer.py:55-66). */
 GDN_API gdn_status gdn_layer_reserve(gdn_layer* layer, int64_t max_tokens);
+
+/* gdn_layer_reserve for calls of up to `max_tokens` rows in at most `max_batch` sequences (a prefill call of
+ * B sequences needs room for B * ceil(T / 64) chunks, at most max_tokens / 64 + max_batch).  With a row limit
+ * (gdn_layer_set_max_rows, set first), max_tokens >= max_rows reserves for calls of any length. */
+GDN_API gdn_status gdn_layer_reserve_batch(gdn_layer* layer, int64_t max_tokens, int32_t max_batch);
+
+/* Row limit for prefill calls: a call of B * T > max_rows rows runs as consecutive pieces of tc tokens of
+ * every sequence (tc = max_rows / B, rounded down to a multiple of 64 when at least 64), each continuing
+ * from the state the previous piece left, so the workspace stays bounded by max_rows rows whatever the
+ * input length; max_rows below the batch is rejected at the call.  0 (the default) = no limit.  Pieces of
+ * more than one sequence are gathered into contiguous rows of the workspace and scattered back.  With
+ * tp_size > 1 every rank must set the same limit (each piece is one all-reduce).  The reference's
+ * constructor argument max_rows and its __call__ loop (9B/gdn_layer.py:55-66, 282-292). */
+GDN_API gdn_status gdn_layer_set_max_rows(gdn_layer* layer, int64_t max_rows);
 
 /* `layer` drops its own workspace and from now on uses `owner`'s (reference counted; it grows to the largest
  * call any sharer makes), so that the layers of a stack hold one workspace between them instead of one each
@@ -134,7 +149,8 @@ GDN_API gdn_status gdn_layer_set_weight_format(gdn_layer* layer, int32_t format)
  * up to 8 MiB, NCCL above).  With comm == NULL the call skips the
  * all-reduce and out holds this rank's partial sum (for callers that reduce themselves).
  * Replaces Qwen35GatedDeltaNetTT.__call__ / _forward_rows (9B/gdn_layer.py:244-292) and
- * Qwen35_08B_GDNStackL1.forward_device (0.8B/gdn_l1.py:295-307).  x may alias nothing else. */
+ * Qwen35_08B_GDNStackL1.forward_device (0.8B/gdn_l1.py:295-307).  x may alias nothing else.  The device
+ * the layer was created on must be current (GDN_ERR_INVALID_ARGUMENT otherwise, before any launch). */
 GDN_API gdn_status gdn_layer_forward(gdn_layer* layer, const uint16_t* x, int32_t batch, int32_t seq_len, float* rec_state,
                              float* conv_state, uint16_t* out, gdn_comm* comm, void* stream);
 
@@ -153,8 +169,10 @@ GDN_API gdn_status gdn_layer_set_stage_events(gdn_layer* layer, void* const* eve
  * every GPU loading this library keeps until exit; a batch whose intermediates do not fit
  * (batch * (4 * proj_ld + 2 * Hv_local * 128) bytes, about 145 sequences for the 9B geometry) is rejected
  * with GDN_ERR_INVALID_ARGUMENT.  The first call on each device looks up the array's device address; make
- * that first call before any stream capture.  All calls share the one array: calls whose GPU work overlaps
- * (different streams, or different layers on concurrent streams) race on it. */
+ * that first call before any stream capture.  The address is looked up again after the device's context
+ * was reset (cudaDeviceReset), so the first call after a reset is a first call too.  All calls share the one
+ * array: calls whose GPU work overlaps (different streams, or different layers on concurrent streams) race
+ * on it.  The device the layer was created on must be current. */
 GDN_API gdn_status gdn_layer_decode_static(gdn_layer* layer, const uint16_t* x, int32_t batch, float* rec_state,
                                            float* conv_state, uint16_t* out, void* stream);
 
@@ -183,7 +201,9 @@ GDN_API gdn_status gdn_comm_create(const void* id, size_t id_bytes, int32_t rank
 GDN_API gdn_status gdn_comm_destroy(gdn_comm* comm);
 
 /* Synchronises the current device and returns (and clears) the device error word that bounded waits
- * inside the kernels set; 0 = no error. */
+ * inside the kernels set; 0 = no error.  After a peer-wait code (0x105: an NVLink all-reduce gave up
+ * waiting for another rank) the ranks' call epochs of that communicator may disagree: destroy the
+ * communicator on every rank and create a new one before the next tensor-parallel call. */
 GDN_API gdn_status gdn_device_error(int32_t* code_out);
 
 /* Failure-detection self-test: one thread waits, with the all-reduce's bounded peer wait, until the u64 at

@@ -24,7 +24,7 @@ EXPORTED = (
     "gdn_recurrence_forward", "gdn_comm_get_unique_id", "gdn_comm_create", "gdn_comm_destroy",
     "gdn_device_error", "gdn_last_error_string", "gdn_kernel_launch_count", "gdn_abi_version", "gdn_gemm_bf16",
     "gdn_layer_set_stage_events", "gdn_layer_decode_static", "gdn_layer_share_workspace",
-    "gdn_layer_set_weight_format", "gdn_selftest_peer_wait",
+    "gdn_layer_set_weight_format", "gdn_selftest_peer_wait", "gdn_layer_reserve_batch", "gdn_layer_set_max_rows",
 )
 
 
@@ -82,6 +82,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gdn_layer_share_workspace": [P, P],
         "gdn_layer_set_weight_format": [P, I32],
         "gdn_selftest_peer_wait": [P, ctypes.c_uint64, P],
+        "gdn_layer_reserve_batch": [P, I64, I32],
+        "gdn_layer_set_max_rows": [P, I64],
     }
     for name, args in sigs.items():
         fn = getattr(lib, name)

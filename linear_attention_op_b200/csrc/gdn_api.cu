@@ -192,6 +192,7 @@ struct gdn_layer {
   WsBlock* ws = nullptr;            // never null after gdn_layer_create
   cudaEvent_t stage_events[7] = {};  // optional stage timing (gdn_layer_set_stage_events)
   int n_stage_events = 0;
+  int64_t max_rows = 0;             // prefill row limit per launch sequence (gdn_layer_set_max_rows); 0 = none
 };
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
@@ -215,11 +216,29 @@ static WsLayout ws_layout(const gdn_layer* L, int64_t n, int64_t chunks, bool f8
   o.total = o.q8 + (f8 ? q8_bytes(L, n) : 0);
   return o;
 }
-static size_t workspace_bytes(const gdn_layer* L, int64_t n, int64_t chunks, bool f8) {
-  return ws_layout(L, n, chunks, f8).total;
+// Row-limited prefill (gdn_layer_set_max_rows): the token range [t0, t0 + tc) of every sequence is one piece
+// of B * tc rows.  Pieces of more than one sequence are gathered into contiguous staging rows (x, then out)
+// placed after the piece's own workspace layout.
+struct PiecePlan {
+  int tc = 0;            // tokens per sequence per piece
+  int64_t rows = 0;      // B * tc
+  int64_t chunks = 0;    // B * ceil(tc / 64)
+  size_t stage = 0;      // offset of the staging rows in the workspace (0: no staging, B == 1)
+  size_t total = 0;      // workspace bytes the split call needs
+};
+static PiecePlan piece_plan(const gdn_layer* L, int B) {
+  PiecePlan p;
+  p.tc = static_cast<int>(std::min<int64_t>(L->max_rows / B, INT32_MAX));
+  if (p.tc >= 64) p.tc &= ~63;  // pieces end where a single call's chunks would end
+  p.rows = static_cast<int64_t>(B) * p.tc;
+  p.chunks = static_cast<int64_t>(B) * ((p.tc + 63) / 64);
+  const size_t base = ws_layout(L, p.rows, p.chunks, L->w_in8 != nullptr).total;
+  const size_t xrows = align256(static_cast<size_t>(p.rows) * L->dims.hidden * 2);
+  p.stage = B > 1 ? base : 0;
+  p.total = base + (B > 1 ? 2 * xrows : 0);
+  return p;
 }
-static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream, bool f8 = false) {
-  const size_t need = workspace_bytes(L, n, chunks, f8);
+static gdn_status ensure_bytes(gdn_layer* L, size_t need, int64_t n, cudaStream_t stream) {
   WsBlock* w = L->ws;
   if (need <= w->bytes) return GDN_OK;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -233,6 +252,9 @@ static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cuda
   GDN_CUDA(cudaMalloc(&w->ptr, need));
   w->bytes = need;
   return GDN_OK;
+}
+static gdn_status ensure_workspace(gdn_layer* L, int64_t n, int64_t chunks, cudaStream_t stream, bool f8 = false) {
+  return ensure_bytes(L, ws_layout(L, n, chunks, f8).total, n, stream);
 }
 
 static void release_ws(WsBlock* w) {
@@ -380,11 +402,34 @@ extern "C" gdn_status gdn_layer_get_info(const gdn_layer* L, gdn_layer_info* inf
   return GDN_OK;
 }
 
+extern "C" gdn_status gdn_layer_reserve_batch(gdn_layer* L, int64_t max_tokens, int32_t max_batch) {
+  if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_reserve_batch: null layer");
+  if (max_tokens <= 0 || max_batch <= 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens %lld and max_batch %d must be > 0",
+                static_cast<long long>(max_tokens), max_batch);
+  // A prefill call of B sequences of T tokens has B * ceil(T / 64) <= B * T / 64 + B chunks.  With a row
+  // limit, a reservation of at least max_rows rows covers calls of any length: longer calls run in pieces
+  // of at most max_rows rows plus their staging rows.
+  int64_t rows = max_tokens;
+  size_t stage = 0;
+  if (L->max_rows > 0 && rows >= L->max_rows) {
+    rows = L->max_rows;
+    if (max_batch > 1) stage = 2 * align256(static_cast<size_t>(rows) * L->dims.hidden * 2);
+  }
+  return ensure_bytes(L, ws_layout(L, rows, rows / 64 + max_batch, L->w_in8 != nullptr).total + stage, max_tokens,
+                      nullptr);
+}
+
 extern "C" gdn_status gdn_layer_reserve(gdn_layer* L, int64_t max_tokens) {
   if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_reserve: null layer");
-  if (max_tokens <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens must be > 0");
-  // prefill chunks: B * ceil(T / 64) <= max_tokens / 64 + B; room for up to 64 ragged sequences
-  return ensure_workspace(L, max_tokens, max_tokens / 64 + 64, nullptr, L->w_in8 != nullptr);
+  return gdn_layer_reserve_batch(L, max_tokens, 64);
+}
+
+extern "C" gdn_status gdn_layer_set_max_rows(gdn_layer* L, int64_t max_rows) {
+  if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_set_max_rows: null layer");
+  if (max_rows < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_rows %lld must be >= 0", static_cast<long long>(max_rows));
+  L->max_rows = max_rows;
+  return GDN_OK;
 }
 
 extern "C" gdn_status gdn_layer_set_weight_format(gdn_layer* L, int32_t format) {
@@ -529,18 +574,20 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   return GDN_OK;
 }
 
-extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t B, int32_t T, float* rec_state,
-                                        float* conv_state, uint16_t* out, gdn_comm* comm, void* stream_ptr) {
-  if (!L || !x || !rec_state || !conv_state || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_forward: null argument");
-  if (B <= 0 || T <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch %d and seq_len %d must be > 0", B, T);
-  if (!aligned16(x) || !aligned16(out) || !aligned16(rec_state) || !aligned16(conv_state))
-    return fail(GDN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
-  if (L->tp_size > 1 && comm) {
-    if (comm->world != L->tp_size || comm->rank != L->tp_rank)
-      return fail(GDN_ERR_INVALID_ARGUMENT, "communicator rank %d/%d does not match layer rank %d/%d", comm->rank,
-                  comm->world, L->tp_rank, L->tp_size);
-  }
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+// The layer's buffers (weights, workspace, static scratch) belong to the device it was created on; a call
+// made with another device current would hand them to kernels running elsewhere.
+static gdn_status check_device(const gdn_layer* L, const char* fn) {
+  int dev = -1;
+  GDN_CUDA(cudaGetDevice(&dev));
+  if (dev != L->device)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "%s: the layer lives on device %d but device %d is current", fn, L->device,
+                dev);
+  return GDN_OK;
+}
+
+// One layer call over B * T contiguous rows, no row limit.
+static gdn_status forward_rows(gdn_layer* L, const uint16_t* x, int B, int T, float* rec_state, float* conv_state,
+                               uint16_t* out, gdn_comm* comm, cudaStream_t stream) {
   const int64_t n = static_cast<int64_t>(B) * T;
   const int64_t chunks = T > 1 ? static_cast<int64_t>(B) * ((T + 63) / 64) : 0;
   const bool f8 = T == 1 && L->w_in8;
@@ -628,6 +675,53 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
   return GDN_OK;
 }
 
+extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t B, int32_t T, float* rec_state,
+                                        float* conv_state, uint16_t* out, gdn_comm* comm, void* stream_ptr) {
+  if (!L || !x || !rec_state || !conv_state || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_forward: null argument");
+  if (B <= 0 || T <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch %d and seq_len %d must be > 0", B, T);
+  if (!aligned16(x) || !aligned16(out) || !aligned16(rec_state) || !aligned16(conv_state))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  if (L->tp_size > 1 && comm) {
+    if (comm->world != L->tp_size || comm->rank != L->tp_rank)
+      return fail(GDN_ERR_INVALID_ARGUMENT, "communicator rank %d/%d does not match layer rank %d/%d", comm->rank,
+                  comm->world, L->tp_rank, L->tp_size);
+  }
+  gdn_status st = check_device(L, "gdn_layer_forward");
+  if (st != GDN_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int64_t n = static_cast<int64_t>(B) * T;
+  if (T == 1 || L->max_rows <= 0 || n <= L->max_rows)
+    return forward_rows(L, x, B, T, rec_state, conv_state, out, comm, stream);
+
+  // Row limit: tokens [t0, t0 + tc) of all B sequences per piece, the state carried from piece to piece
+  // (the reference's __call__ loop over max_rows // batch tokens, 9B/gdn_layer.py:282-292).
+  if (L->max_rows < B)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "max_rows %lld is below the batch %d", static_cast<long long>(L->max_rows),
+                B);
+  const PiecePlan p = piece_plan(L, B);
+  st = ensure_bytes(L, p.total, p.rows, stream);
+  if (st != GDN_OK) return st;
+  const int64_t h = L->dims.hidden;
+  char* ws = static_cast<char*>(L->ws->ptr);
+  uint16_t* xs = p.stage ? reinterpret_cast<uint16_t*>(ws + p.stage) : nullptr;
+  uint16_t* os = p.stage ? reinterpret_cast<uint16_t*>(ws + p.stage + align256(static_cast<size_t>(p.rows) * h * 2))
+                         : nullptr;
+  for (int t0 = 0; t0 < T; t0 += p.tc) {
+    const int tl = std::min(p.tc, T - t0);
+    const size_t row_bytes = static_cast<size_t>(tl) * h * 2, seq_pitch = static_cast<size_t>(T) * h * 2;
+    if (p.stage) {
+      GDN_CUDA(cudaMemcpy2DAsync(xs, row_bytes, x + t0 * h, seq_pitch, row_bytes, B, cudaMemcpyDeviceToDevice, stream));
+      st = forward_rows(L, xs, B, tl, rec_state, conv_state, os, comm, stream);
+      if (st != GDN_OK) return st;
+      GDN_CUDA(cudaMemcpy2DAsync(out + t0 * h, seq_pitch, os, row_bytes, row_bytes, B, cudaMemcpyDeviceToDevice, stream));
+    } else {
+      st = forward_rows(L, x + t0 * h, 1, tl, rec_state, conv_state, out + t0 * h, comm, stream);
+      if (st != GDN_OK) return st;
+    }
+  }
+  return GDN_OK;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Decode step with static scratch (gdn_layer_decode_static)
 //
@@ -642,23 +736,59 @@ static constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 
 static constexpr int kMaxDevices = 64;
-static void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+  void* ptr = nullptr;
+  unsigned long long ctx_id = 0;  // the context the address belongs to (0: not looked up)
+};
+static ScratchAddr g_scratch_addr[kMaxDevices];
 static std::mutex g_scratch_mu;
 
-// Device address of g_decode_scratch on the current device, looked up once per device (the host-side
-// symbol is only a stand-in and must never be handed to a kernel).
+// Unique id of the current CUDA context (cuCtxGetId, reached through the runtime's driver entry points so
+// the library needs no link-time libcuda).  A context reset (cudaDeviceReset) makes a new context with a
+// new id, so an address cached for the old one is looked up again instead of being reused.
+typedef int (*CtxGetCurrentFn)(void** ctx);
+typedef int (*CtxGetIdFn)(void* ctx, unsigned long long* id);
+static gdn_status current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return fail(GDN_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId are unavailable");
+  void* ctx = nullptr;
+  if (get_current(&ctx) != 0 || !ctx || get_id(ctx, id) != 0)
+    return fail(GDN_ERR_CUDA, "no current CUDA context");
+  return GDN_OK;
+}
+
+// Device address of g_decode_scratch on the current device: looked up once per device and context, with
+// that device current (the host-side symbol is only a stand-in and must never be handed to a kernel).
 static gdn_status static_scratch(void** out) {
   int dev = 0;
   GDN_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(GDN_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  GDN_CUDA(cudaSetDevice(dev));  // binds the device's primary context to this thread before reading its id
+  unsigned long long ctx = 0;
+  gdn_status st = current_context_id(&ctx);
+  if (st != GDN_OK) return st;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  ScratchAddr& a = g_scratch_addr[dev];
+  if (!a.ptr || a.ctx_id != ctx) {
     void* p = nullptr;
     GDN_CUDA(cudaGetSymbolAddress(&p, g_decode_scratch));
     if (!p) return fail(GDN_ERR_CUDA, "cudaGetSymbolAddress returned null for the static scratch");
-    g_scratch_addr[dev] = p;
+    a.ptr = p;
+    a.ctx_id = ctx;
   }
-  *out = g_scratch_addr[dev];
+  *out = a.ptr;
   return GDN_OK;
 }
 
@@ -679,8 +809,10 @@ extern "C" gdn_status gdn_layer_decode_static(gdn_layer* L, const uint16_t* x, i
                 "(at most %zu sequences for this layer)",
                 B, need, kStaticScratchBytes,
                 kStaticScratchBytes / (static_cast<size_t>(L->proj_ld) * 4 + static_cast<size_t>(L->vd) * 2));
+  gdn_status st = check_device(L, "gdn_layer_decode_static");
+  if (st != GDN_OK) return st;
   void* base = nullptr;
-  gdn_status st = static_scratch(&base);
+  st = static_scratch(&base);
   if (st != GDN_OK) return st;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const int h = L->dims.hidden;

@@ -128,8 +128,11 @@ class _LayerHandle:
         call("gdn_layer_get_info", self.handle, ctypes.byref(self.info))
         self.hidden = w.hidden
 
-    def reserve(self, max_tokens: int) -> None:
-        call("gdn_layer_reserve", self.handle, int(max_tokens))
+    def reserve(self, max_tokens: int, max_batch: int = 64) -> None:
+        call("gdn_layer_reserve_batch", self.handle, int(max_tokens), int(max_batch))
+
+    def set_max_rows(self, max_rows: int) -> None:
+        call("gdn_layer_set_max_rows", self.handle, int(max_rows))
 
     def forward(self, x: torch.Tensor, B: int, T: int, rec: torch.Tensor, conv: torch.Tensor, out: torch.Tensor,
                 comm=None, stream=None) -> None:
@@ -184,8 +187,15 @@ class Qwen35GatedDeltaNet:
         self.conv_dim_local = info.conv_dim_local
         self.dk = self.dv = HEAD_DIM
         if max_rows:
+            # the reference's max_rows (9B/gdn_layer.py:55-66, 282-292): longer prefill calls run in pieces of
+            # at most max_rows rows, and the workspace is reserved for them once
+            if max_rows < batch:
+                raise ValueError(f"max_rows {max_rows} must be >= batch {batch}")
+            self._h.set_max_rows(max_rows)
             with torch.cuda.device(self.device):
-                self._h.reserve(max_rows)
+                self._h.reserve(max_rows, batch)
+        self.max_rows = max_rows
+        self._io = None
         self.reset_state()
 
     # ---- state (9B/gdn_layer.py:137-157) -----------------------------------------------------------
@@ -235,9 +245,47 @@ class Qwen35GatedDeltaNet:
             self.forward_into(x, out)
             return _to_caller(out, hidden_states, pinned)
 
-    def reserve(self, max_tokens: int) -> None:
+    def forward_host_async(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.cuda.Event:
+        """Pinned host bf16 x [B, T, hidden] -> pinned host bf16 out, without waiting: the host-to-device copy,
+        the layer call and the device-to-host copy are queued and the returned event completes when out_host
+        holds the result.  Copies run on two copy streams with double-buffered device rows, so a call's
+        input copy overlaps the previous call's compute and its result copy the next call's compute (the
+        calls themselves stay in order on the current stream).  x_host must not change, and out_host must
+        not be read, before the event completes."""
+        B, T, H = x_host.shape
+        if B != self.batch or H != self.hidden or tuple(out_host.shape) != (B, T, H):
+            raise ValueError(f"x {tuple(x_host.shape)} / out {tuple(out_host.shape)} do not match [{self.batch}, T, {self.hidden}]")
+        if x_host.dtype != torch.bfloat16 or out_host.dtype != torch.bfloat16 or not (x_host.is_pinned() and out_host.is_pinned()):
+            raise ValueError("forward_host_async wants pinned host bf16 tensors")
         with torch.cuda.device(self.device):
-            self._h.reserve(max_tokens)
+            io = self._io
+            if io is None or io["shape"] != (B, T, H):
+                dev = lambda: torch.empty(B, T, H, dtype=torch.bfloat16, device=self.device)
+                io = self._io = {"shape": (B, T, H), "xin": [dev(), dev()], "xout": [dev(), dev()], "i": 0,
+                                 "h2d_stream": torch.cuda.Stream(self.device), "d2h_stream": torch.cuda.Stream(self.device),
+                                 "h2d": [torch.cuda.Event(), torch.cuda.Event()], "d2h": [torch.cuda.Event(), torch.cuda.Event()],
+                                 "done": [torch.cuda.Event(), torch.cuda.Event()]}
+            i = io["i"]
+            io["i"] = i ^ 1
+            cur = torch.cuda.current_stream()
+            hs, ds = io["h2d_stream"], io["d2h_stream"]
+            hs.wait_event(io["done"][i])  # the call that last read xin[i] has finished
+            with torch.cuda.stream(hs):
+                io["xin"][i].copy_(x_host, non_blocking=True)
+                io["h2d"][i].record(hs)
+            cur.wait_event(io["h2d"][i])
+            cur.wait_event(io["d2h"][i])  # the copy that last read xout[i] has finished
+            self.forward_into(io["xin"][i], io["xout"][i], stream=cur)
+            io["done"][i].record(cur)
+            ds.wait_event(io["done"][i])
+            with torch.cuda.stream(ds):
+                out_host.copy_(io["xout"][i], non_blocking=True)
+                io["d2h"][i].record(ds)
+            return io["d2h"][i]
+
+    def reserve(self, max_tokens: int, max_batch: int | None = None) -> None:
+        with torch.cuda.device(self.device):
+            self._h.reserve(max_tokens, max_batch if max_batch is not None else max(self.batch, 64))
 
     def share_workspace(self, owner: "Qwen35GatedDeltaNet") -> None:
         """Use owner's device workspace instead of this layer's own (gdn_layer_share_workspace); the two
@@ -256,6 +304,7 @@ class Qwen35GatedDeltaNet:
         other.__dict__.update({k: v for k, v in self.__dict__.items() if k not in ("rec_state", "conv_state")})
         other.batch = batch
         other.rec_state = other.conv_state = None
+        other._io = None
         other.reset_state()
         return other
 
@@ -290,7 +339,12 @@ class GDNStack:
         for L in self.layers[1:]:
             L.share_workspace(self.layers[0])
         if max_rows:
-            self.layers[0].reserve(max_rows)
+            if max_rows < batch:
+                raise ValueError(f"max_rows {max_rows} must be >= batch {batch}")
+            for L in self.layers:
+                L._h.set_max_rows(max_rows)
+                L.max_rows = max_rows
+            self.layers[0].reserve(max_rows, batch)
         self.hidden = self.layers[0].hidden
         self.device = self.layers[0].device
 

@@ -1,4 +1,4 @@
-"""The allocation-free decode entry point (gdn_layer_decode_static) against gdn_layer_forward.
+"""The allocation-free decode entry point (gdn_layer_decode_static) against gdn_layer_forward and the oracle.
 
 Some callers cannot allocate device memory while they call the layer: a serving runtime that owns the
 GPU's memory budget, or code that issues the call while a stream is being captured (a cudaMalloc there
@@ -49,6 +49,12 @@ def test_static_decode_matches_forward_two_calls(hidden, hk, hv, B):
         check(f"static decode call {t}", got[t], want[t])
     check("static decode state", layer.rec_state, want_s, max_rel=STATE_TOL)
     check("static decode conv state", layer.conv_state, want_c, max_rel=1e-4)
+    # and against the CPU oracle on the same inputs and starting state
+    with torch.no_grad():
+        o_want, o_s, o_c = O.layer_forward(w, xs.float().cpu(), rec_state=s0, conv_state=c0, mode="recurrent")
+    check("static decode vs oracle", torch.cat(got, 1), o_want)
+    check("static decode state vs oracle", layer.rec_state, o_s, max_rel=STATE_TOL)
+    check("static decode conv state vs oracle", layer.conv_state, o_c, max_rel=1e-4)
 
 
 def test_static_decode_rejects_batch_beyond_scratch():
