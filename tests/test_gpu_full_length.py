@@ -39,10 +39,10 @@ def test_config2_all_256_decode_steps():
     layer = Qwen35GatedDeltaNet(weights=w, batch=B)
     layer.set_state(rec_state=s0)
     xd = x.to("cuda", torch.bfloat16)
-    outs = torch.empty(B, steps, 4096, dtype=torch.bfloat16, device="cuda")
+    outs = torch.empty(steps, B, 1, 4096, dtype=torch.bfloat16, device="cuda")
     for t in range(steps):
-        layer.forward_into(xd[:, t:t + 1].contiguous(), outs[:, t:t + 1])
-    got = outs.float().cpu()
+        layer.forward_into(xd[:, t:t + 1].contiguous(), outs[t])
+    got = outs[:, :, 0].transpose(0, 1).float().cpu()
     assert device_error() == 0
     with torch.no_grad():
         want, s, c = O.layer_forward(w, x, rec_state=s0, mode="recurrent")
