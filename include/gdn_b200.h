@@ -176,6 +176,37 @@ GDN_API gdn_status gdn_layer_set_stage_events(gdn_layer* layer, void* const* eve
 GDN_API gdn_status gdn_layer_decode_static(gdn_layer* layer, const uint16_t* x, int32_t batch, float* rec_state,
                                            float* conv_state, uint16_t* out, void* stream);
 
+/* ---- The decoder layer around the mixer --------------------------------------------------------------
+ * A Qwen3.5 decoder layer of the linear-attention type (Hugging Face Qwen3_5DecoderLayer.forward):
+ *   h = x + mixer(RMSNorm(x) * (1 + w_in));   out = h + down(SiLU(gate(n)) * up(n)),  n = RMSNorm(h) * (1 + w_post)
+ * The reference stacks GDN mixers only (0.8B/gdn_l1.py:295-325) and names these surroundings -- input
+ * RMSNorm, residual, MLP -- as its next step (0.8B/OPTIMIZATION.md:258-259). */
+typedef struct gdn_mlp_weights {
+  const float* input_norm_w;  /* fp32 [hidden]                 input_layernorm.weight (applied as 1 + w) */
+  const float* post_norm_w;   /* fp32 [hidden]                 post_attention_layernorm.weight           */
+  const uint16_t* w_gate;     /* bf16 [intermediate, hidden]   mlp.gate_proj.weight                      */
+  const uint16_t* w_up;       /* bf16 [intermediate, hidden]   mlp.up_proj.weight                        */
+  const uint16_t* w_down;     /* bf16 [hidden, intermediate]   mlp.down_proj.weight                      */
+  int32_t intermediate;       /* a multiple of 64 * tp_size */
+  float eps;                  /* rms_norm_eps */
+} gdn_mlp_weights;
+
+typedef struct gdn_decoder gdn_decoder; /* opaque */
+
+/* A decoder layer around `mixer` (which stays owned by the caller and must outlive it), on the mixer's
+ * device and tensor-parallel shard: the MLP is split by intermediate columns (gate/up rows, down columns),
+ * giving a partial output that one more all-reduce sums.  Pointers may be host or device memory. */
+GDN_API gdn_status gdn_decoder_create(gdn_layer* mixer, const gdn_mlp_weights* weights, gdn_decoder** out_decoder);
+GDN_API gdn_status gdn_decoder_destroy(gdn_decoder* decoder);
+/* Pre-allocate the decoder's own workspace for calls of up to max_tokens rows (the mixer's is reserved with
+ * gdn_layer_reserve / gdn_layer_reserve_batch). */
+GDN_API gdn_status gdn_decoder_reserve(gdn_decoder* decoder, int64_t max_tokens);
+/* One decoder-layer call, continuing the mixer's state like gdn_layer_forward (T == 1 decode, T > 1
+ * prefill).  out bf16 [B, T, hidden] must not alias x.  With tp_size > 1, comm is required (the post-mixer
+ * norm needs the full mixer output) and every rank receives the full output: two all-reduces per call. */
+GDN_API gdn_status gdn_decoder_forward(gdn_decoder* decoder, const uint16_t* x, int32_t batch, int32_t seq_len,
+                                       float* rec_state, float* conv_state, uint16_t* out, gdn_comm* comm, void* stream);
+
 /* Recurrence only (no projections, conv or norm), token by token, state updated in place:
  *   q, k fp32 [B, T, Hk, 128]; v fp32 [B, T, Hv, 128]; g (log decay), beta fp32 [B, T, Hv];
  *   state fp32 [B, Hv, 128, 128]; o fp32 [B, T, Hv, 128].

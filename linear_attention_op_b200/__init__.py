@@ -5,7 +5,8 @@ chunked prefill); this package is the host-side mirror of the reference's per-la
 """
 
 from ._lib import GDNError, GDNLibraryError, device_error, launch_count, lib  # noqa: F401
-from .gdn_layer import GatedDeltaRule, GDNStack, LayerWeights, Qwen35GatedDeltaNet  # noqa: F401
+from .gdn_layer import (  # noqa: F401
+    DecoderMlpWeights, GatedDeltaRule, GDNStack, LayerWeights, Qwen35DecoderLayer, Qwen35GatedDeltaNet)
 
-__all__ = ["Qwen35GatedDeltaNet", "GDNStack", "GatedDeltaRule", "LayerWeights", "GDNError", "GDNLibraryError",
-           "device_error", "launch_count", "lib"]
+__all__ = ["Qwen35GatedDeltaNet", "Qwen35DecoderLayer", "DecoderMlpWeights", "GDNStack", "GatedDeltaRule",
+           "LayerWeights", "GDNError", "GDNLibraryError", "device_error", "launch_count", "lib"]

@@ -25,6 +25,7 @@ EXPORTED = (
     "gdn_device_error", "gdn_last_error_string", "gdn_kernel_launch_count", "gdn_abi_version", "gdn_gemm_bf16",
     "gdn_layer_set_stage_events", "gdn_layer_decode_static", "gdn_layer_share_workspace",
     "gdn_layer_set_weight_format", "gdn_selftest_peer_wait", "gdn_layer_reserve_batch", "gdn_layer_set_max_rows",
+    "gdn_decoder_create", "gdn_decoder_destroy", "gdn_decoder_reserve", "gdn_decoder_forward",
 )
 
 
@@ -49,6 +50,12 @@ class Dims(ctypes.Structure):
 class Weights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in
                 ("w_qkv", "w_z", "w_a", "w_b", "conv_w", "a_log", "dt_bias", "norm_w", "w_out")]
+
+
+class MlpWeights(ctypes.Structure):
+    _fields_ = [("input_norm_w", ctypes.c_void_p), ("post_norm_w", ctypes.c_void_p), ("w_gate", ctypes.c_void_p),
+                ("w_up", ctypes.c_void_p), ("w_down", ctypes.c_void_p), ("intermediate", ctypes.c_int32),
+                ("eps", ctypes.c_float)]
 
 
 class LayerInfo(ctypes.Structure):
@@ -83,6 +90,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gdn_layer_set_weight_format": [P, I32],
         "gdn_selftest_peer_wait": [P, ctypes.c_uint64, P],
         "gdn_layer_reserve_batch": [P, I64, I32],
+        "gdn_decoder_create": [P, ctypes.POINTER(MlpWeights), ctypes.POINTER(P)],
+        "gdn_decoder_destroy": [P],
+        "gdn_decoder_reserve": [P, I64],
+        "gdn_decoder_forward": [P, P, I32, I32, P, P, P, P, P],
         "gdn_layer_set_max_rows": [P, I64],
     }
     for name, args in sigs.items():

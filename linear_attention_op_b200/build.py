@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libgdn_b200.so"
-SOURCES = ["gemm.cu", "recurrence.cu", "conv.cu", "chunk_tc.cu", "allreduce.cu", "gdn_api.cu"]
+SOURCES = ["gemm.cu", "recurrence.cu", "conv.cu", "chunk_tc.cu", "allreduce.cu", "decoder.cu", "gdn_api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr"]

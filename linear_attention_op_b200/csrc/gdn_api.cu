@@ -585,6 +585,42 @@ static gdn_status check_device(const gdn_layer* L, const char* fn) {
   return GDN_OK;
 }
 
+// Decode outputs up to the slot size go through the NVLink all-reduce: the GEMM that produced the partial
+// wrote it into this rank's slot for this call (GemmEpiArgs.slot_epoch).
+static bool p2p_eligible(const gdn_comm* comm, int tp_size, int T, int64_t out_elems) {
+  return T == 1 && tp_size > 1 && comm && comm->p2p && out_elems % 8 == 0 &&
+         static_cast<size_t>(out_elems) * 2 <= kP2PSlotBytes;
+}
+static unsigned long long* p2p_epoch_word(gdn_comm* comm) {
+  return comm ? reinterpret_cast<unsigned long long*>(comm->sym) + 2 * kP2PMaxRanks : nullptr;
+}
+
+// Sum of the ranks' bf16 partials into `out` on every rank: the NVLink kernel (partials in the slots) or
+// ncclAllReduce in place (partial in `out`).
+static gdn_status allreduce_out(gdn_comm* comm, uint16_t* out, int64_t out_elems, bool p2p, cudaStream_t stream) {
+  if (p2p) {
+    P2PAllReduceArgs ar;
+    for (int p = 0; p < comm->world; ++p) {
+      ar.src[p] = comm->peer[p] + kP2PSlotOffset;
+      ar.flags[p] = reinterpret_cast<unsigned long long*>(comm->peer[p]);
+    }
+    ar.epoch = p2p_epoch_word(comm);
+    ar.cta_done = reinterpret_cast<unsigned int*>(ar.epoch + 1);
+    ar.out = out;
+    ar.n = out_elems;
+    ar.slot_bytes = static_cast<int64_t>(kP2PSlotBytes);
+    ar.rank = comm->rank;
+    ar.world = comm->world;
+    GDN_CUDA(allreduce_p2p(ar, stream));
+    return GDN_OK;
+  }
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  ncclResult_t r = api.allReduce(out, out, static_cast<size_t>(out_elems), ncclBfloat16, ncclSum, comm->comm, stream);
+  if (r != ncclSuccess) return fail(GDN_ERR_NCCL, "ncclAllReduce: %s", api.getErrorString(r));
+  return GDN_OK;
+}
+
 // One layer call over B * T contiguous rows, no row limit.
 static gdn_status forward_rows(gdn_layer* L, const uint16_t* x, int B, int T, float* rec_state, float* conv_state,
                                uint16_t* out, gdn_comm* comm, cudaStream_t stream) {
@@ -605,9 +641,8 @@ static gdn_status forward_rows(gdn_layer* L, const uint16_t* x, int B, int T, fl
   // Tensor parallel: decode outputs are reduced by the NVLink all-reduce, so out_proj writes this rank's
   // partial into the communicator's mapped slot for this call; prefill outputs by NCCL in place.
   const int64_t out_elems = n * h;
-  const bool p2p = T == 1 && L->tp_size > 1 && comm && comm->p2p && out_elems % 8 == 0 &&
-                   static_cast<size_t>(out_elems) * 2 <= kP2PSlotBytes;
-  unsigned long long* p2p_epoch = comm ? reinterpret_cast<unsigned long long*>(comm->sym) + 2 * kP2PMaxRanks : nullptr;
+  const bool p2p = p2p_eligible(comm, L->tp_size, T, out_elems);
+  unsigned long long* p2p_epoch = p2p_epoch_word(comm);
 
   GDN_CUDA(stage_mark(L, 0, stream));
   if (T == 1) {
@@ -651,25 +686,9 @@ static gdn_status forward_rows(gdn_layer* L, const uint16_t* x, int B, int T, fl
     GDN_CUDA(gemm_bf16_persistent(y, L->vd, L->w_out, static_cast<int>(n), h, L->vd, kEpiStoreBF16, eo, stream, true));
     GDN_CUDA(stage_mark(L, 5, stream));
   }
-  if (p2p) {
-    P2PAllReduceArgs ar;
-    for (int p = 0; p < comm->world; ++p) {
-      ar.src[p] = comm->peer[p] + kP2PSlotOffset;
-      ar.flags[p] = reinterpret_cast<unsigned long long*>(comm->peer[p]);
-    }
-    ar.epoch = p2p_epoch;
-    ar.cta_done = reinterpret_cast<unsigned int*>(ar.epoch + 1);
-    ar.out = out;
-    ar.n = out_elems;
-    ar.slot_bytes = static_cast<int64_t>(kP2PSlotBytes);
-    ar.rank = comm->rank;
-    ar.world = comm->world;
-    GDN_CUDA(allreduce_p2p(ar, stream));
-  } else if (L->tp_size > 1 && comm) {
-    const NcclApi& api = nccl();
-    if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
-    ncclResult_t r = api.allReduce(out, out, static_cast<size_t>(n) * h, ncclBfloat16, ncclSum, comm->comm, stream);
-    if (r != ncclSuccess) return fail(GDN_ERR_NCCL, "ncclAllReduce: %s", api.getErrorString(r));
+  if (L->tp_size > 1 && comm) {
+    const gdn_status ar = allreduce_out(comm, out, out_elems, p2p, stream);
+    if (ar != GDN_OK) return ar;
   }
   GDN_CUDA(stage_mark(L, 6, stream));
   return GDN_OK;
@@ -719,6 +738,173 @@ extern "C" gdn_status gdn_layer_forward(gdn_layer* L, const uint16_t* x, int32_t
       if (st != GDN_OK) return st;
     }
   }
+  return GDN_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Decoder layer around the mixer (gdn_decoder_*): input RMSNorm -> GDN mixer -> residual -> post RMSNorm
+// -> SwiGLU MLP -> residual, the linear-attention layer type of HF Qwen3_5DecoderLayer.forward.
+// ------------------------------------------------------------------------------------------------
+struct gdn_decoder {
+  gdn_layer* mixer = nullptr;        // not owned
+  int hidden = 0, inter = 0, inter_local = 0;
+  float eps = 1e-6f;
+  float* norm_in = nullptr;          // [hidden], applied as (1 + w)
+  float* norm_post = nullptr;        // [hidden]
+  __nv_bfloat16* w_gu = nullptr;     // [2 * inter_local, hidden], row 2j = gate_j, 2j + 1 = up_j; pre-tiled
+  __nv_bfloat16* w_down = nullptr;   // [hidden, inter_local] (this rank's columns), pre-tiled
+  WsBlock* ws = nullptr;             // xn / hn [n, hidden] | mixer output [n, hidden] | act [n, inter_local]
+};
+
+static void free_decoder(gdn_decoder* D) {
+  if (!D) return;
+  for (void* p : {static_cast<void*>(D->norm_in), static_cast<void*>(D->norm_post), static_cast<void*>(D->w_gu),
+                  static_cast<void*>(D->w_down)})
+    if (p) cudaFree(p);
+  release_ws(D->ws);
+  delete D;
+}
+
+extern "C" gdn_status gdn_decoder_create(gdn_layer* mixer, const gdn_mlp_weights* w, gdn_decoder** out) {
+  if (!mixer || !w || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_decoder_create: null argument");
+  *out = nullptr;
+  if (!w->input_norm_w || !w->post_norm_w || !w->w_gate || !w->w_up || !w->w_down)
+    return fail(GDN_ERR_NULL_POINTER, "gdn_decoder_create: a weight pointer is null");
+  const int G = mixer->tp_size, r = mixer->tp_rank, h = mixer->dims.hidden, I = w->intermediate;
+  if (I <= 0 || I % G) return fail(GDN_ERR_INVALID_ARGUMENT, "intermediate %d must be a positive multiple of tp_size %d", I, G);
+  if ((I / G) % 64) return fail(GDN_ERR_UNSUPPORTED, "intermediate per rank %d must be a multiple of 64", I / G);
+  if (h > 8192) return fail(GDN_ERR_UNSUPPORTED, "hidden %d above 8192", h);
+  if (!(w->eps > 0.f)) return fail(GDN_ERR_INVALID_ARGUMENT, "eps must be > 0");
+  gdn_status st = check_device(mixer, "gdn_decoder_create");
+  if (st != GDN_OK) return st;
+  gdn_decoder* D = new (std::nothrow) gdn_decoder();
+  if (!D) return fail(GDN_ERR_OUT_OF_MEMORY, "host allocation failed");
+  D->ws = new (std::nothrow) WsBlock();
+  if (!D->ws) {
+    delete D;
+    return fail(GDN_ERR_OUT_OF_MEMORY, "host allocation failed");
+  }
+  D->mixer = mixer;
+  D->hidden = h;
+  D->inter = I;
+  D->inter_local = I / G;
+  D->eps = w->eps;
+  const int64_t il = D->inter_local, i0 = static_cast<int64_t>(r) * il;
+  __nv_bfloat16 *gu_rm = nullptr, *down_rm = nullptr;
+  auto run = [&]() -> gdn_status {
+    GDN_CUDA(cudaMalloc(&D->norm_in, h * 4));
+    GDN_CUDA(cudaMalloc(&D->norm_post, h * 4));
+    GDN_CUDA(cudaMemcpy(D->norm_in, w->input_norm_w, h * 4, cudaMemcpyDefault));
+    GDN_CUDA(cudaMemcpy(D->norm_post, w->post_norm_w, h * 4, cudaMemcpyDefault));
+    GDN_CUDA(cudaMalloc(&gu_rm, 2 * il * h * 2));
+    GDN_CUDA(cudaMalloc(&down_rm, static_cast<size_t>(h) * il * 2));
+    // gate rows of this rank's columns to the even rows, up rows to the odd rows
+    GDN_CUDA(cudaMemcpy2D(gu_rm, 2 * h * 2, w->w_gate + i0 * h, h * 2, h * 2, il, cudaMemcpyDefault));
+    GDN_CUDA(cudaMemcpy2D(reinterpret_cast<char*>(gu_rm) + h * 2, 2 * h * 2, w->w_up + i0 * h, h * 2, h * 2, il,
+                          cudaMemcpyDefault));
+    GDN_CUDA(cudaMemcpy2D(down_rm, il * 2, w->w_down + i0, static_cast<size_t>(I) * 2, il * 2, h, cudaMemcpyDefault));
+    GDN_CUDA(cudaMalloc(&D->w_gu, tiled_weight_bytes(static_cast<int>(2 * il), h)));
+    GDN_CUDA(cudaMalloc(&D->w_down, tiled_weight_bytes(h, static_cast<int>(il))));
+    GDN_CUDA(tile_weights_bf16(gu_rm, h, static_cast<int>(2 * il), h, D->w_gu, nullptr));
+    GDN_CUDA(tile_weights_bf16(down_rm, il, h, static_cast<int>(il), D->w_down, nullptr));
+    GDN_CUDA(cudaDeviceSynchronize());
+    return GDN_OK;
+  };
+  st = run();
+  if (gu_rm) cudaFree(gu_rm);
+  if (down_rm) cudaFree(down_rm);
+  if (st != GDN_OK) {
+    free_decoder(D);
+    return st;
+  }
+  *out = D;
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_decoder_destroy(gdn_decoder* D) {
+  if (!D) return fail(GDN_ERR_NULL_POINTER, "gdn_decoder_destroy: null decoder");
+  free_decoder(D);
+  return GDN_OK;
+}
+
+static size_t decoder_ws_bytes(const gdn_decoder* D, int64_t n) {
+  return 2 * align256(static_cast<size_t>(n) * D->hidden * 2) + align256(static_cast<size_t>(n) * D->inter_local * 2);
+}
+
+extern "C" gdn_status gdn_decoder_reserve(gdn_decoder* D, int64_t max_tokens) {
+  if (!D) return fail(GDN_ERR_NULL_POINTER, "gdn_decoder_reserve: null decoder");
+  if (max_tokens <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "max_tokens must be > 0");
+  WsBlock* w = D->ws;
+  const size_t need = decoder_ws_bytes(D, max_tokens);
+  if (need <= w->bytes) return GDN_OK;
+  if (w->ptr) GDN_CUDA(cudaFree(w->ptr));
+  w->ptr = nullptr;
+  w->bytes = 0;
+  GDN_CUDA(cudaMalloc(&w->ptr, need));
+  w->bytes = need;
+  return GDN_OK;
+}
+
+extern "C" gdn_status gdn_decoder_forward(gdn_decoder* D, const uint16_t* x, int32_t B, int32_t T, float* rec_state,
+                                          float* conv_state, uint16_t* out, gdn_comm* comm, void* stream_ptr) {
+  if (!D || !x || !rec_state || !conv_state || !out) return fail(GDN_ERR_NULL_POINTER, "gdn_decoder_forward: null argument");
+  if (B <= 0 || T <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch %d and seq_len %d must be > 0", B, T);
+  if (!aligned16(x) || !aligned16(out)) return fail(GDN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  if (x == out) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_decoder_forward: out must not alias x");
+  gdn_layer* L = D->mixer;
+  if (L->tp_size > 1 && !comm)
+    return fail(GDN_ERR_INVALID_ARGUMENT,
+                "a tensor-parallel decoder layer needs its communicator (the post-mixer norm reads the full sum)");
+  gdn_status st = check_device(L, "gdn_decoder_forward");
+  if (st != GDN_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int64_t n = static_cast<int64_t>(B) * T;
+  const int h = D->hidden;
+  const int il = D->inter_local;
+  const size_t need = decoder_ws_bytes(D, n);
+  if (need > D->ws->bytes) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+      return fail(GDN_ERR_INVALID_ARGUMENT, "decoder workspace for %lld rows is not reserved (gdn_decoder_reserve)",
+                  static_cast<long long>(n));
+    st = gdn_decoder_reserve(D, n);
+    if (st != GDN_OK) return st;
+  }
+  char* ws = static_cast<char*>(D->ws->ptr);
+  const size_t rows_bytes = align256(static_cast<size_t>(n) * h * 2);
+  uint16_t* xn = reinterpret_cast<uint16_t*>(ws);
+  uint16_t* mixed = reinterpret_cast<uint16_t*>(ws + rows_bytes);
+  __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(ws + 2 * rows_bytes);
+  // input RMSNorm -> mixer (its own all-reduce) -> h = x + mixer output (into out) and its post RMSNorm
+  GDN_CUDA(rmsnorm_rows(x, nullptr, nullptr, D->norm_in, D->eps, xn, static_cast<int>(n), h, stream));
+  st = gdn_layer_forward(L, xn, B, T, rec_state, conv_state, mixed, comm, stream);
+  if (st != GDN_OK) return st;
+  GDN_CUDA(rmsnorm_rows(x, mixed, out, D->norm_post, D->eps, xn, static_cast<int>(n), h, stream));
+  // SwiGLU MLP; the residual h (in out) is added by rank 0's down-projection epilogue, before the sum
+  const bool p2p = p2p_eligible(comm, L->tp_size, T, n * h);
+  GemmEpiArgs eg;
+  eg.out = act;
+  eg.ld = il;
+  GemmEpiArgs ed;
+  ed.ld = h;
+  ed.residual = L->tp_rank == 0 ? out : nullptr;
+  ed.res_ld = h;
+  if (T == 1) {
+    eg.a_tiled = D->w_gu;
+    GDN_CUDA(gemm_bf16_tn(D->w_gu, h, xn, h, 2 * il, B, h, kEpiSwiGLUT, eg, 0, stream, true));
+    ed.a_tiled = D->w_down;
+    ed.out = p2p ? static_cast<void*>(comm->sym + kP2PSlotOffset) : static_cast<void*>(out);
+    ed.slot_epoch = p2p ? p2p_epoch_word(comm) : nullptr;
+    ed.slot_bytes = p2p ? static_cast<int64_t>(kP2PSlotBytes) : 0;
+    GDN_CUDA(gemm_bf16_tn(D->w_down, il, act, il, h, B, il, kEpiStoreBF16T, ed, 0, stream, true));
+  } else {
+    eg.b_tiled = D->w_gu;
+    GDN_CUDA(gemm_bf16_persistent(xn, h, D->w_gu, static_cast<int>(n), 2 * il, h, kEpiSwiGLU, eg, stream, true));
+    ed.out = out;
+    ed.b_tiled = D->w_down;
+    GDN_CUDA(gemm_bf16_persistent(act, il, D->w_down, static_cast<int>(n), h, il, kEpiStoreBF16, ed, stream, true));
+  }
+  if (L->tp_size > 1) return allreduce_out(comm, out, n * h, p2p, stream);
   return GDN_OK;
 }
 

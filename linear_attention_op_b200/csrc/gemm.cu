@@ -52,6 +52,19 @@ struct GemmCfg {
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0, int M, int N,
                                            const float (&v)[16]) {
+  if constexpr (EPI == kEpiSwiGLUT) {
+    // Rows 2j (gate) and 2j + 1 (up) sit in neighbouring lanes: every lane of the warp takes part in the
+    // exchange (M is even, so both rows of a pair are in range or neither is).
+    float u[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) u[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
+    if (m >= M || (m & 1)) return;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(ep.out);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + (m >> 1)] = __float2bfloat16_rn(silu_fast(v[j]) * u[j]);
+    return;
+  }
   if (m >= M) return;
   if constexpr (EPI == kEpiStoreF32) {
     float* row = static_cast<float*>(ep.out) + static_cast<int64_t>(m) * ep.ld + n0;
@@ -88,9 +101,18 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
       if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = v[j];
   } else if constexpr (EPI == kEpiStoreBF16T) {
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(ep.out);
+    if (ep.residual) {
+      const __nv_bfloat16* res = static_cast<const __nv_bfloat16*>(ep.residual);
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = __float2bfloat16_rn(v[j]);
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N)
+          out[static_cast<int64_t>(n0 + j) * ep.ld + m] =
+              __float2bfloat16_rn(v[j] + __bfloat162float(res[static_cast<int64_t>(n0 + j) * ep.res_ld + m]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = __float2bfloat16_rn(v[j]);
+    }
   } else {  // kEpiDecodeInProj
     float* out = static_cast<float*>(ep.out);
     const int cr = ep.conv_rows;
@@ -179,7 +201,8 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap& tmA, const CUten
   if (warp == 0) {
     if (elect_one()) {
       // Decode (transposed epilogues): A is the weight matrix, streamed exactly once.
-      const bool a_streamed = EPI == kEpiStoreF32T || EPI == kEpiStoreBF16T || EPI == kEpiDecodeInProj;
+      const bool a_streamed = EPI == kEpiStoreF32T || EPI == kEpiStoreBF16T || EPI == kEpiDecodeInProj ||
+                              EPI == kEpiSwiGLUT;
       const uint64_t pol_a = a_streamed ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = policy_evict_last();
       // The weight operand (A for the transposed decode epilogues, B otherwise) does not depend on the
@@ -487,6 +510,7 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
     case kEpiStoreF32T: return launch_gemm<BN, STAGES, kEpiStoreF32T>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     case kEpiDecodeInProj: return launch_gemm<BN, STAGES, kEpiDecodeInProj>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiSwiGLUT: return launch_gemm<BN, STAGES, kEpiSwiGLUT>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -494,6 +518,8 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
 cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, int epi,
                          const GemmEpiArgs& ep, int ksplit, cudaStream_t stream, bool pdl, bool trigger) {
   if (M <= 0 || N <= 0 || K <= 0 || (K & 7)) return cudaErrorInvalidValue;
+  if (epi == kEpiSwiGLUT && (M & 1)) return cudaErrorInvalidValue;
+  if (ep.residual && (epi != kEpiStoreBF16T || ep.res_ld < M)) return cudaErrorInvalidValue;
   int BN;
   if (N <= 16) BN = 16;
   else if (N <= 32) BN = 32;
@@ -1007,8 +1033,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __syncwarp();
   } else {
     griddep_wait();  // the epilogue writes buffers the previous kernel may still read
-    constexpr int kOutBytes = EPI == kEpiStoreBF16 ? 2 : 4;
-    constexpr int kChunk = 64 / kOutBytes;  // columns per 64-byte staged row: 16 (fp32) or 32 (bf16)
+    constexpr bool kSwiGLU = EPI == kEpiSwiGLU;
+    constexpr int kOutBytes = (EPI == kEpiStoreBF16 || kSwiGLU) ? 2 : 4;
+    // accumulator columns per 64-byte staged output row: 16 (fp32), 32 (bf16), 64 (SwiGLU: gate/up pairs)
+    constexpr int kChunk = kSwiGLU ? 64 : 64 / kOutBytes;
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;       // column half [128 half, +128) of each tile
     const int r = q * 32 + lane;
@@ -1039,8 +1067,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll 1
       for (int c0 = half * (kPBN / 2); c0 < (half + 1) * (kPBN / 2); c0 += kChunk) {
         float v[kChunk];
-        tmem_ld16(t_row + c0, *reinterpret_cast<float(*)[16]>(v));
-        if constexpr (kChunk == 32) tmem_ld16(t_row + c0 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+#pragma unroll
+        for (int c16 = 0; c16 < kChunk / 16; ++c16)
+          tmem_ld16(t_row + c0 + 16 * c16, *reinterpret_cast<float(*)[16]>(v + 16 * c16));
         const int n0 = nt * kPBN + c0;
         if (issuer) bulk_wait_read();  // the previous store has read the staging rows
         bool done = false;
@@ -1060,10 +1089,33 @@ __global__ void __launch_bounds__(kPThreads, 1)
               c[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
                                 __float_as_uint(v[4 * i + 3]));
           } else {
+            float o[32];
+            if constexpr (kSwiGLU) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = silu_fast(v[2 * i]) * v[2 * i + 1];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = v[i];
+              if (ep.residual && store) {  // bf16(acc + residual) of this row's 32 columns
+                const uint4* rr = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(ep.residual) +
+                                                                 static_cast<int64_t>(row) * ep.res_ld + n0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const uint4 rv = rr[i];
+                  const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const float2 f = __bfloat1622float2(rh[j]);
+                    o[8 * i + 2 * j] += f.x;
+                    o[8 * i + 2 * j + 1] += f.y;
+                  }
+                }
+              }
+            }
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
               w[i] = *reinterpret_cast<uint32_t*>(&h2);
             }
 #pragma unroll
@@ -1074,7 +1126,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         fence_proxy_async_shared();
         epi_half_sync(half);
         if (issuer) {
-          tma_store_2d(&tmOut, stage, n0, mt * m_stride);
+          tma_store_2d(&tmOut, stage, kSwiGLU ? n0 / 2 : n0, mt * m_stride);
           bulk_commit();
         }
       }
@@ -1172,8 +1224,14 @@ cudaError_t gemm_bf16_persistent(const void* A, int64_t lda, const void* B_tiled
       if ((e = make_out_tmap(&to, ep.out, M, N, ep.ld, false, 16, kBM)) != cudaSuccess) return e;
       return launch_persistent<kEpiStoreF32>(ta, to, B_tiled, M, N, K, kBM, ep, pdl, stream);
     case kEpiStoreBF16:
+      if (ep.residual && (ep.res_ld < N || (ep.res_ld & 7) || (reinterpret_cast<uintptr_t>(ep.residual) & 15) || (N & 31)))
+        return cudaErrorInvalidValue;
       if ((e = make_out_tmap(&to, ep.out, M, N, ep.ld, true, 32, kBM)) != cudaSuccess) return e;
       return launch_persistent<kEpiStoreBF16>(ta, to, B_tiled, M, N, K, kBM, ep, pdl, stream);
+    case kEpiSwiGLU:
+      if ((N & 1) || ep.residual) return cudaErrorInvalidValue;
+      if ((e = make_out_tmap(&to, ep.out, M, N / 2, ep.ld, true, 32, kBM)) != cudaSuccess) return e;
+      return launch_persistent<kEpiSwiGLU>(ta, to, B_tiled, M, N, K, kBM, ep, pdl, stream);
     case kEpiPrefillInProj:
       if (ep.seq_len <= 0 || ep.conv_rows <= 0 || (ep.conv_rows & 15) || ep.conv_rows > N || (ep.ld & 3) ||
           (M % ep.seq_len) || !ep.conv_w || !ep.conv_state || !ep.conv_tail ||

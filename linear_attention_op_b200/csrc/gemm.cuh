@@ -19,6 +19,10 @@ enum GemmEpi : int {
   kEpiPrefillInProj = 5, // row-major fp32 store of the prefill in_proj (rows = tokens of seq_len-token
                          // sequences); columns [0, conv_rows) get the causal conv (K = 4) + SiLU, the
                          // raw last 3 inputs of each sequence go to conv_tail (persistent kernel only)
+  kEpiSwiGLUT = 6,       // decode MLP gate/up (A = weights with gate and up rows interleaved: row 2j gate_j,
+                         // row 2j + 1 up_j): out[n * ld + j] = bf16(SiLU(acc[2j][n]) * acc[2j + 1][n])
+  kEpiSwiGLU = 7,        // prefill MLP gate/up (B = the interleaved weights): out[m * ld + j] =
+                         // bf16(SiLU(acc[m][2j]) * acc[m][2j + 1]) (persistent kernel only)
 };
 
 struct GemmEpiArgs {
@@ -46,6 +50,11 @@ struct GemmEpiArgs {
   // gemm_f8_tn only: acc[m][n] is multiplied by row_scale[m] * col_scale[n] (the operands' e4m3 scales)
   const float* row_scale = nullptr;
   const float* col_scale = nullptr;
+  // kEpiStoreBF16T (gemm_bf16_tn) and kEpiStoreBF16 (gemm_bf16_persistent): when set, the stored value is
+  // bf16(acc + residual) with residual bf16 in the output's layout, row stride res_ld (may alias `out`:
+  // every element is read and then written by the same thread).
+  const void* residual = nullptr;
+  int64_t res_ld = 0;
 };
 
 // A: [M, K] bf16 row-major with row stride lda (elements); B: [N, K] bf16 row-major with row stride ldb
@@ -63,8 +72,8 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
 
 // Persistent variant for the large prefill projections: one CTA per SM, 128 x 256 tiles, two TMEM
 // accumulators so a tile's epilogue overlaps the next tile's MMAs.  A [M, K] bf16 row-major (row stride
-// lda); B_tiled = weights [N, K] pre-tiled by tile_weights_bf16.  epi: kEpiStoreF32, kEpiStoreBF16 or
-// kEpiPrefillInProj.
+// lda); B_tiled = weights [N, K] pre-tiled by tile_weights_bf16.  epi: kEpiStoreF32, kEpiStoreBF16,
+// kEpiPrefillInProj or kEpiSwiGLU (N even; out is [M, N / 2]).
 cudaError_t gemm_bf16_persistent(const void* A, int64_t lda, const void* B_tiled, int M, int N, int K, int epi,
                                  const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false);
 

@@ -82,6 +82,12 @@ size_t chunk_prefill_scratch_bytes(int B, int T, int Hk, int Hv);
 cudaError_t chunk_prep(const ChunkArgs& a, void* scratch, cudaStream_t stream);
 cudaError_t chunk_state(const ChunkArgs& a, const void* scratch, cudaStream_t stream);
 
+// Decoder-layer RMSNorm (Qwen3_5RMSNorm: fp32 normalisation, times (1 + w), bf16 out) of `rows` rows of h
+// bf16; with `add`, the rows are first summed with it (bf16 residual add) and, with `sum_out`, that sum is
+// stored too.  Pointers 16-byte aligned, h a multiple of 8 and at most 8192.  Programmatic dependent launch.
+cudaError_t rmsnorm_rows(const void* x, const void* add, void* sum_out, const float* w, float eps, void* out, int rows,
+                         int h, cudaStream_t stream);
+
 // NVLink all-reduce (sum) of bf16 [n] partials: src[p] is rank p's first slot (own included, mapped into this
 // process; the second follows slot_bytes later), flags[p] rank p's flag page: arrive[kP2PMaxRanks] u64
 // counters at [0], reduced[kP2PMaxRanks][kP2PMaxCtas] at [kP2PReducedOff].  epoch and cta_done[2] are this

@@ -6,6 +6,9 @@
   back with one state per layer, ``layers=[i]`` selection, ``allocate_activations`` / ``forward_into``
   for CUDA-graph replay (the reference's trace capture, 0.8B/bench_decode.py:44-57).
 * ``GatedDeltaRule``       <- ``GatedDeltaRuleL1`` (9B/gated_delta_l1.py:131-272): the recurrence alone.
+* ``Qwen35DecoderLayer``   <- Hugging Face ``Qwen3_5DecoderLayer`` of the linear-attention type: input RMSNorm,
+  the mixer, residual, post RMSNorm, SwiGLU MLP, residual (the surroundings the reference names as its next
+  step, 0.8B/OPTIMIZATION.md:258-259).
 
 Everything runs in libgdn_b200.so; PyTorch only provides device memory and the current stream.  Errors
 raise ``GDNError`` (the reference uses asserts / ValueError, which callers may also catch as RuntimeError).
@@ -19,7 +22,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import Dims, LayerInfo, Weights, call
+from ._lib import Dims, LayerInfo, MlpWeights, Weights, call
 
 HEAD_DIM = 128
 
@@ -420,3 +423,102 @@ class GatedDeltaRule:
                  1 if use_qk_l2norm else 0, float(scale) if scale else 0.0, _ptr(self.state), _ptr(o),
                  _stream_handle())
         return o.to(q.device)
+
+
+@dataclass
+class DecoderMlpWeights:
+    """The decoder layer's weights around the mixer (host or device tensors): RMSNorm weights [hidden]
+    (applied as 1 + w), gate/up [intermediate, hidden], down [hidden, intermediate]."""
+
+    input_norm_w: torch.Tensor
+    post_norm_w: torch.Tensor
+    w_gate: torch.Tensor
+    w_up: torch.Tensor
+    w_down: torch.Tensor
+    eps: float = 1e-6
+
+    @classmethod
+    def from_hf(cls, layer) -> "DecoderMlpWeights":
+        """From a Hugging Face ``Qwen3_5DecoderLayer`` (linear-attention type)."""
+        g = lambda t: t.detach()
+        return cls(g(layer.input_layernorm.weight), g(layer.post_attention_layernorm.weight),
+                   g(layer.mlp.gate_proj.weight), g(layer.mlp.up_proj.weight), g(layer.mlp.down_proj.weight),
+                   float(layer.input_layernorm.eps))
+
+
+class Qwen35DecoderLayer:
+    """A whole Qwen3.5 decoder layer of the linear-attention type on a B200, continuing from the mixer's
+    on-device state across calls: ``layer(x)`` with x ``[B, T, hidden]`` returns ``[B, T, hidden]``
+    (T == 1 decode, T > 1 prefill), as HF ``Qwen3_5DecoderLayer`` with its cache does.  ``mixer`` is the
+    ``Qwen35GatedDeltaNet`` inside (its state, ``reset_state``, ``get_recurrent_state``, weight format and row
+    limit).  With ``tp_size > 1`` a communicator is required: every rank gets the full output."""
+
+    def __init__(self, hf_layer=None, batch: int = 1, *, mixer_weights=None, mlp_weights=None, device=None,
+                 tp_rank: int = 0, tp_size: int = 1, comm=None, max_rows: int | None = None,
+                 weight_dtype: str = "bf16"):
+        if hf_layer is not None:
+            mixer_weights, mlp_weights = hf_layer.linear_attn, DecoderMlpWeights.from_hf(hf_layer)
+        if mixer_weights is None or mlp_weights is None:
+            raise ValueError("pass hf_layer, or mixer_weights and mlp_weights")
+        if tp_size > 1 and comm is None:
+            raise ValueError("a tensor-parallel decoder layer needs its communicator")
+        self.mixer = Qwen35GatedDeltaNet(weights=mixer_weights, batch=batch, device=device, tp_rank=tp_rank,
+                                         tp_size=tp_size, comm=comm, max_rows=max_rows, weight_dtype=weight_dtype)
+        self.device, self.batch, self.hidden, self.comm = self.mixer.device, batch, self.mixer.hidden, comm
+        m = mlp_weights
+        bf = lambda t: t.detach().to(torch.bfloat16).contiguous()
+        f32 = lambda t: t.detach().to(torch.float32).contiguous()
+        keep = dict(input_norm_w=f32(m.input_norm_w), post_norm_w=f32(m.post_norm_w), w_gate=bf(m.w_gate),
+                    w_up=bf(m.w_up), w_down=bf(m.w_down))
+        self.intermediate = int(keep["w_gate"].shape[0])
+        cw = MlpWeights(*(ctypes.c_void_p(keep[k].data_ptr()) for k in
+                          ("input_norm_w", "post_norm_w", "w_gate", "w_up", "w_down")), self.intermediate, float(m.eps))
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("gdn_decoder_create", self.mixer._h.handle, ctypes.byref(cw), ctypes.byref(handle))
+            if max_rows:
+                call("gdn_decoder_reserve", handle, int(max_rows))
+        self.handle = handle
+
+    # state: the mixer's
+    def reset_state(self) -> None:
+        self.mixer.reset_state()
+
+    def set_state(self, rec_state=None, conv_state=None) -> None:
+        self.mixer.set_state(rec_state, conv_state)
+
+    def get_recurrent_state(self) -> torch.Tensor:
+        return self.mixer.get_recurrent_state()
+
+    def get_conv_state(self) -> torch.Tensor:
+        return self.mixer.get_conv_state()
+
+    def forward_into(self, x: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+        """Device bf16 x [B, T, hidden] -> device bf16 out (preallocated, not aliasing x)."""
+        B, T, H = x.shape
+        if B != self.batch or H != self.hidden:
+            raise ValueError(f"x is {tuple(x.shape)}, layer expects [{self.batch}, T, {self.hidden}]")
+        if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or not x.is_contiguous() or not out.is_contiguous():
+            raise ValueError("forward_into wants contiguous bf16 tensors")
+        mx = self.mixer
+        call("gdn_decoder_forward", self.handle, _ptr(x), B, T, _ptr(mx.rec_state), _ptr(mx.conv_state), _ptr(out),
+             ctypes.c_void_p(self.comm.handle.value if self.comm is not None else 0), _stream_handle(stream))
+        return out
+
+    def __call__(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        with torch.cuda.device(self.device):
+            x, pinned = _to_device(hidden_states, self.device)
+            out = torch.empty_like(x)
+            self.forward_into(x, out)
+            return _to_caller(out, hidden_states, pinned)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            _lib.lib().gdn_decoder_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
