@@ -349,14 +349,23 @@ def swiglu_mlp(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down
 
 
 def decoder_layer_forward(dw: DecoderWeights, x: torch.Tensor, rec_state=None, conv_state=None,
-                          mode: str = "recurrent", chunk: int = 64):
+                          mode: str = "recurrent", chunk: int = 64, bf16_acts: bool = False):
     """One decoder-layer call that continues from (rec_state, conv_state), in fp32; returns
-    (out [B, T, hidden], new rec_state, new conv_state)."""
+    (out [B, T, hidden], new rec_state, new conv_state).
+
+    bf16_acts: the activations between the steps are rounded to bf16 as a bf16 HF model stores them --
+    ``Qwen3_5RMSNorm.forward`` casts its result back to the input dtype (``output.type_as(x)``), the mixer
+    returns its out_proj output in that dtype and the residual sums of ``Qwen3_5DecoderLayer.forward`` run in
+    it; the MLP's SiLU(gate) * up product is rounded before the down projection.  The recurrent state still
+    evolves in fp32 from the rounded mixer input."""
+    r = bf16_round if bf16_acts else (lambda t: t)
     x = x.float()
-    mixed, S, conv = layer_forward(dw.gdn, rmsnorm_offset(x, dw.input_norm_w, dw.eps), rec_state, conv_state,
+    mixed, S, conv = layer_forward(dw.gdn, r(rmsnorm_offset(x, dw.input_norm_w, dw.eps)), rec_state, conv_state,
                                    mode=mode, chunk=chunk)
-    h = x + mixed
-    out = h + swiglu_mlp(rmsnorm_offset(h, dw.post_norm_w, dw.eps), dw.w_gate, dw.w_up, dw.w_down)
+    h = r(x + r(mixed))
+    hn = r(rmsnorm_offset(h, dw.post_norm_w, dw.eps))
+    act = r(F.silu(hn @ dw.w_gate.float().T) * (hn @ dw.w_up.float().T))
+    out = h + act @ dw.w_down.float().T
     return out, S, conv
 
 
