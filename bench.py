@@ -459,6 +459,11 @@ def run_ours(args):
         result["parity"] = parity
     if args.prefill:
         result["prefill"] = run_prefill(args, layer, dev, world, pk)
+    if args.stack:
+        del graph, layer
+        graph = None
+        torch.cuda.empty_cache()
+        result["stack"] = run_stack(args, rank, world, comm, dev, pk)
     if device_error() != 0:
         raise SystemExit("device error during the benchmark")
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -521,6 +526,76 @@ def run_prefill(args, layer_dec, dev, world, pk):
         "recurrence_tflops": round(fl["recurrence"] / (rec_ms * 1e-3) / 1e12, 2),
         "clocks": clk.summary(),
     }
+
+
+def run_stack(args, rank, world, comm, dev, pk):
+    """Config 4: a stack of 24 Qwen3.5-9B GDN layers (random init, per-layer seeds, A_log = log U(1, 64)),
+    batch 128, a 4096-token prefill then 512 decode steps, head-parallel over the N GPUs (fixed total work:
+    strong scaling).  The layers share one workspace, bounded by a 65536-row limit (the prefill runs in
+    pieces of 512 tokens of all 128 sequences); every decode step of the whole stack is ONE CUDA-graph
+    replay (24 layers, one all-reduce each)."""
+    from linear_attention_op_b200 import GDNStack
+
+    L, B, T0, steps = args.stack_layers, 128, args.stack_prefill, args.stack_steps
+    weights = [synthetic_weights(1000 + i, dev, a_max=64.0) for i in range(L)]
+    stack = GDNStack(weights, batch=B, device=dev, tp_rank=rank, tp_size=world, comm=comm, max_rows=65536)
+    del weights
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(B, T0, H, generator=g, device=dev).to(torch.bfloat16)
+    bufs = [torch.empty_like(x), torch.empty_like(x)]
+    outs = [bufs[i % 2] for i in range(L)]
+    xd = torch.randn(B, 1, H, generator=g, device=dev).to(torch.bfloat16)
+    douts = [torch.empty_like(xd) for _ in range(2)]
+    dlist = [douts[i % 2] for i in range(L)]
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    wb = [torch.empty(B, 128, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    with torch.cuda.stream(stream):  # warm-up: a short prefill and a decode step, then back to zero state
+        stack.forward_into(x[:, :128].contiguous(), [wb[i % 2] for i in range(L)], stream=stream)
+        stack.forward_into(xd, dlist, stream=stream)
+    del wb
+    torch.cuda.synchronize()
+    stack.reset_state()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        stack.forward_into(x, outs, stream=stream)
+        ev[1].record(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        stack.forward_into(xd, dlist, stream=stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        if world > 1:
+            graph.replay()  # lines the ranks' devices up (its all-reduces); one extra untimed step
+        ev[2].record(stream)
+        for _ in range(steps):
+            graph.replay()
+        ev[3].record(stream)
+    torch.cuda.synchronize()
+    pre_ms = max_over_ranks(ev[0].elapsed_time(ev[1]), world)
+    dec_ms = max_over_ranks(ev[2].elapsed_time(ev[3]), world)
+    del graph
+    byt = decode_bytes(B, world)["step"] * L  # per GPU per step
+    fl = prefill_flops(B, T0, world)["step"] * L
+    res = {
+        "workload": f"cfg4: {L} Qwen3.5-9B GDN layers, batch {B}, {T0}-token prefill then {steps} decode steps, "
+                    f"A_log = log U(1,64), tp{world} head-parallel",
+        "scaling": "strong", "prefill_ms": round(pre_ms, 2), "prefill_tokens_per_s": round(B * T0 / (pre_ms / 1e3), 1),
+        "prefill_tflops": round(fl / (pre_ms * 1e-3) / 1e12, 1),
+        "decode_ms_per_step": round(dec_ms / steps, 4), "decode_tokens_per_s": round(B * steps / (dec_ms / 1e3), 1),
+        "decode_step_gbs_per_gpu": round(byt / (dec_ms / steps * 1e-3) / 1e9, 1),
+        "decode_step_hbm_frac": round(byt / (dec_ms / steps * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+        "tokens_per_s": round(B * (T0 + steps) / ((pre_ms + dec_ms) / 1e3), 1),
+        "graph": f"one CUDA graph per decode step of all {L} layers",
+        "prefill_row_limit": 65536,
+    }
+    del stack
+    return res
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -591,6 +666,10 @@ def main():
     ap.add_argument("--graph-steps", type=int, default=16, help="decode steps captured per CUDA graph")
     ap.add_argument("--prefill-b", type=int, default=PREFILL_B)
     ap.add_argument("--prefill-t", type=int, default=PREFILL_T)
+    ap.add_argument("--no-stack", dest="stack", action="store_false", help="skip the config-4 stack line")
+    ap.add_argument("--stack-layers", type=int, default=24)
+    ap.add_argument("--stack-prefill", type=int, default=4096)
+    ap.add_argument("--stack-steps", type=int, default=512)
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
                     help="fp8: e4m3 projection weights and decode activations (not the benchmark config's "
                          "bf16 weights; reported beside it)")
@@ -598,6 +677,8 @@ def main():
     globals()["DECODE_B"], globals()["PREFILL_B"], globals()["PREFILL_T"] = args.decode_b, args.prefill_b, args.prefill_t
     if args.only == "decode":
         args.prefill = False
+    if args.only != "all":
+        args.stack = False
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
