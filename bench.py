@@ -263,7 +263,7 @@ def max_abs_rel(got: torch.Tensor, want: torch.Tensor) -> float:
     return float((got - want).abs().max() / want.abs().max().clamp_min(1e-30))
 
 
-def tp_parity(layer, W, rank: int, world: int, dev) -> dict:
+def tp_parity(layer, W, rank: int, world: int, dev, weight_dtype: str = "bf16") -> dict:
     """Multi-GPU correctness, checked before the timed region: the head-parallel layer (this rank's shard and
     the library communicator) against a single-GPU layer (tp_size 1, the path the GPU test suite pins to the
     CPU oracle) built from the same weights on this rank's GPU, on the same inputs.
@@ -281,7 +281,7 @@ def tp_parity(layer, W, rank: int, world: int, dev) -> dict:
     conv_idx = torch.cat([torch.arange(k0, k0 + kd), HK * D + torch.arange(k0, k0 + kd),
                           2 * HK * D + torch.arange(v0, v0 + vd)]).to(dev)
     B = layer.batch
-    ref = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev)
+    ref = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev, weight_dtype=weight_dtype)
     g = torch.Generator(device=dev).manual_seed(77)  # identical on every rank
     s0 = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.1
     c0 = torch.randn(B, 3, 2 * HK * D + HV * D, generator=g, device=dev)
@@ -349,7 +349,7 @@ def run_ours(args):
         if comm is not None:
             comm.close()
         return
-    parity = tp_parity(layer, W, rank, world, dev) if world > 1 and args.weights == "bf16" else None
+    parity = tp_parity(layer, W, rank, world, dev, args.weights) if world > 1 else None
     g = torch.Generator(device=dev).manual_seed(1000 + rank)  # this rank's heads of the N(0, 0.1) state
     layer.set_state(rec_state=torch.randn(B, HV // world, D, D, generator=g, device=dev) * 0.1)
     gx = torch.Generator(device=dev).manual_seed(1)  # the replicated input, identical on every rank
@@ -404,7 +404,7 @@ def run_ours(args):
 
     st = stage_times(layer, dec_step, min(max(args.steps, 20), 50))
     names = STAGES
-    byt = decode_bytes(B, world, 1 if args.weights == "fp8" else 2)
+    byt = decode_bytes(B, world, 1 if args.weights.startswith("fp8") else 2)
     dec_stage = {n: round(t * 1e3, 2) for n, t in zip(names, st) if n not in ("conv", "chunk_prep")}
     dom = max(["in_proj", "recurrence", "out_proj"], key=lambda n: dec_stage[n])
     achieved = byt[dom] / (dec_stage[dom] * 1e-6) / 1e9
@@ -448,8 +448,11 @@ def run_ours(args):
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": ("bf16 (fp32 state, fp32 accumulation)" if args.weights == "bf16" else
-                  "fp8 e4m3 projection weights and decode activations, bf16 elsewhere (fp32 state, fp32 accumulation)"), "data": "synthetic",
+        "vs_baseline": None, "dtype": {
+            "bf16": "bf16 (fp32 state, fp32 accumulation)",
+            "fp8": "fp8 e4m3 projection weights, bf16 activations (fp32 state, fp32 accumulation)",
+            "fp8_w8a8": "fp8 e4m3 projection weights and decode activations, bf16 elsewhere (fp32 state, fp32 accumulation)",
+        }[args.weights], "data": "synthetic",
         "config": workload_config(world),
         "roofline": roofline, "decode": decode_detail, "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step,
@@ -670,9 +673,9 @@ def main():
     ap.add_argument("--stack-layers", type=int, default=24)
     ap.add_argument("--stack-prefill", type=int, default=4096)
     ap.add_argument("--stack-steps", type=int, default=512)
-    ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
-                    help="fp8: e4m3 projection weights and decode activations (not the benchmark config's "
-                         "bf16 weights; reported beside it)")
+    ap.add_argument("--weights", choices=["bf16", "fp8", "fp8_w8a8"], default="bf16",
+                    help="fp8: e4m3 projection weights, bf16 activations; fp8_w8a8: e4m3 decode activations too "
+                         "(not the benchmark config's bf16 weights; reported beside it)")
     args = ap.parse_args()
     globals()["DECODE_B"], globals()["PREFILL_B"], globals()["PREFILL_T"] = args.decode_b, args.prefill_b, args.prefill_t
     if args.only == "decode":

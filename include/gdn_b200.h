@@ -130,16 +130,24 @@ GDN_API gdn_status gdn_layer_share_workspace(gdn_layer* layer, gdn_layer* owner)
 /* Weight formats (the reference's weight_dtype argument: ttnn.bfloat16 / bfloat8_b, 9B/gdn_layer.py:55,90-119,
  * 0.8B/gdn_l1.py:155). */
 enum {
-  GDN_WEIGHTS_BF16 = 0,     /* as created */
-  GDN_WEIGHTS_FP8_E4M3 = 1  /* e4m3 weights with one power-of-two scale per output row */
+  GDN_WEIGHTS_BF16 = 0,             /* as created */
+  GDN_WEIGHTS_FP8_E4M3 = 1,         /* e4m3 weights AND e4m3 decode activations (per-token scales) */
+  GDN_WEIGHTS_FP8_WEIGHT_ONLY = 2   /* e4m3 weights, bf16 activations: the reference's bfloat8_b semantics */
 };
 
-/* Switch a layer's projection weights to `format`.  GDN_WEIGHTS_FP8_E4M3 quantises every output row of the
- * fused in_proj and of out_proj to e4m3 with the smallest power-of-two scale that keeps the row within
- * +-448; decode calls (T == 1) then quantise their activations the same way per token and run the
- * projections as e4m3 x e4m3 tensor-core GEMMs (half the weight bytes streamed per step), and prefill calls
- * use the dequantised weights (exact in bf16) with bf16 activations.  One way: the bf16 originals are not
- * kept.  tp_size 1 only; gdn_layer_decode_static is unavailable for fp8 layers. */
+/* Switch a layer's projection weights to `format` (once; the bf16 originals are not kept).  Both fp8 formats
+ * quantise every output row of the fused in_proj and of out_proj to e4m3 with the smallest power-of-two
+ * scale that keeps the WHOLE row within +-448 (out_proj rows are split across tensor-parallel ranks by
+ * columns; their scales come from the full rows, so every shard quantises exactly as one GPU would).
+ * Prefill calls use the dequantised weights (exact in bf16) with bf16 activations.  Decode calls (T == 1)
+ * stream the e4m3 weights (half the bytes):
+ *   GDN_WEIGHTS_FP8_WEIGHT_ONLY  activations stay bf16; each e4m3 weight stage is widened to bf16 in shared
+ *                                memory for the bf16 tensor cores (the reference quantises weights only:
+ *                                weight_dtype=bfloat8_b, 9B/gdn_layer.py:55,90-119, 0.8B/test_gdn_l1.py:24-52);
+ *                                any tp_size;
+ *   GDN_WEIGHTS_FP8_E4M3         activations are quantised per token to e4m3 too and the projections run as
+ *                                e4m3 x e4m3 tensor-core GEMMs; tp_size 1 only.
+ * gdn_layer_decode_static is unavailable for fp8 layers. */
 GDN_API gdn_status gdn_layer_set_weight_format(gdn_layer* layer, int32_t format);
 
 /* One layer call that continues from (rec_state, conv_state) and updates both in place:

@@ -189,6 +189,8 @@ struct gdn_layer {
   uint8_t* w_out8 = nullptr;
   float* s_in = nullptr;            // [rows]
   float* s_out = nullptr;           // [hidden]
+  int wformat = GDN_WEIGHTS_BF16;   // gdn_layer_set_weight_format
+  float* out_amax = nullptr;        // tp_size > 1: max |W_out| over each WHOLE output row (all ranks' columns)
   WsBlock* ws = nullptr;            // never null after gdn_layer_create
   cudaEvent_t stage_events[7] = {};  // optional stage timing (gdn_layer_set_stage_events)
   int n_stage_events = 0;
@@ -232,7 +234,7 @@ static PiecePlan piece_plan(const gdn_layer* L, int B) {
   if (p.tc >= 64) p.tc &= ~63;  // pieces end where a single call's chunks would end
   p.rows = static_cast<int64_t>(B) * p.tc;
   p.chunks = static_cast<int64_t>(B) * ((p.tc + 63) / 64);
-  const size_t base = ws_layout(L, p.rows, p.chunks, L->w_in8 != nullptr).total;
+  const size_t base = ws_layout(L, p.rows, p.chunks, L->wformat == GDN_WEIGHTS_FP8_E4M3).total;
   const size_t xrows = align256(static_cast<size_t>(p.rows) * L->dims.hidden * 2);
   p.stage = B > 1 ? base : 0;
   p.total = base + (B > 1 ? 2 * xrows : 0);
@@ -269,7 +271,7 @@ static void free_layer(gdn_layer* L) {
   for (void* p : {static_cast<void*>(L->w_in), static_cast<void*>(L->w_out), static_cast<void*>(L->conv_w),
                   static_cast<void*>(L->a_log), static_cast<void*>(L->dt_bias), static_cast<void*>(L->norm_w),
                   static_cast<void*>(L->w_in8), static_cast<void*>(L->w_out8), static_cast<void*>(L->s_in),
-                  static_cast<void*>(L->s_out)})
+                  static_cast<void*>(L->s_out), static_cast<void*>(L->out_amax)})
     if (p) cudaFree(p);
   release_ws(L->ws);
   delete L;
@@ -368,6 +370,19 @@ extern "C" gdn_status gdn_layer_create(const gdn_dims* dims, const gdn_weights* 
                           L->vd * 2, h, cudaMemcpyDefault));
     GDN_CUDA(tile_weights_bf16(w_in_rm, h, L->rows, static_cast<int>(h), L->w_in, nullptr));
     GDN_CUDA(tile_weights_bf16(w_out_rm, L->vd, static_cast<int>(h), L->vd, L->w_out, nullptr));
+    if (tp_size > 1) {
+      // The maxima of out_proj's whole rows, for fp8 weights that every shard quantises alike (its rows are
+      // split by columns across the ranks); the full matrix passes through w_in_rm's space when it fits.
+      GDN_CUDA(cudaMalloc(&L->out_amax, static_cast<size_t>(h) * 4));
+      void* full = nullptr;
+      const size_t fbytes = static_cast<size_t>(h) * vd_g * 2;
+      GDN_CUDA(cudaMalloc(&full, fbytes));
+      cudaError_t e = cudaMemcpy(full, w->w_out, fbytes, cudaMemcpyDefault);
+      if (e == cudaSuccess) e = row_amax_bf16(full, vd_g, static_cast<int>(h), static_cast<int>(vd_g), L->out_amax, nullptr);
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();
+      cudaFree(full);
+      GDN_CUDA(e);
+    }
     GDN_CUDA(cudaDeviceSynchronize());
     return GDN_OK;
   };
@@ -416,7 +431,7 @@ extern "C" gdn_status gdn_layer_reserve_batch(gdn_layer* L, int64_t max_tokens, 
     rows = L->max_rows;
     if (max_batch > 1) stage = 2 * align256(static_cast<size_t>(rows) * L->dims.hidden * 2);
   }
-  return ensure_bytes(L, ws_layout(L, rows, rows / 64 + max_batch, L->w_in8 != nullptr).total + stage, max_tokens,
+  return ensure_bytes(L, ws_layout(L, rows, rows / 64 + max_batch, L->wformat == GDN_WEIGHTS_FP8_E4M3).total + stage, max_tokens,
                       nullptr);
 }
 
@@ -434,13 +449,16 @@ extern "C" gdn_status gdn_layer_set_max_rows(gdn_layer* L, int64_t max_rows) {
 
 extern "C" gdn_status gdn_layer_set_weight_format(gdn_layer* L, int32_t format) {
   if (!L) return fail(GDN_ERR_NULL_POINTER, "gdn_layer_set_weight_format: null layer");
+  if (format == L->wformat) return GDN_OK;
   if (format == GDN_WEIGHTS_BF16)
-    return L->w_in8 ? fail(GDN_ERR_UNSUPPORTED, "the weights are fp8 already (the bf16 originals are not kept)")
-                    : GDN_OK;
-  if (format != GDN_WEIGHTS_FP8_E4M3) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown weight format %d", format);
-  if (L->w_in8) return GDN_OK;
-  if (L->tp_size > 1)
-    return fail(GDN_ERR_UNSUPPORTED, "fp8 weights need tp_size 1 (out_proj row scales would differ per shard)");
+    return fail(GDN_ERR_UNSUPPORTED, "the weights are fp8 already (the bf16 originals are not kept)");
+  if (format != GDN_WEIGHTS_FP8_E4M3 && format != GDN_WEIGHTS_FP8_WEIGHT_ONLY)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "unknown weight format %d", format);
+  if (L->w_in8) return fail(GDN_ERR_UNSUPPORTED, "the weights are fp8 in another mode already");
+  if (L->tp_size > 1 && format == GDN_WEIGHTS_FP8_E4M3)
+    return fail(GDN_ERR_UNSUPPORTED,
+                "fp8 weights with fp8 activations need tp_size 1 (the per-token activation scales of out_proj's "
+                "input would differ per shard); GDN_WEIGHTS_FP8_WEIGHT_ONLY works at any tp_size");
   const int h = L->dims.hidden;
   if (h % 128 || L->vd % 128)
     return fail(GDN_ERR_UNSUPPORTED, "fp8 weights need hidden and value width multiples of 128");
@@ -453,7 +471,7 @@ extern "C" gdn_status gdn_layer_set_weight_format(gdn_layer* L, int32_t format) 
   if (e == cudaSuccess) e = cudaMalloc(&s_in, static_cast<size_t>(L->rows) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s_out, static_cast<size_t>(h) * 4);
   if (e == cudaSuccess) e = quantize_tiled_weights_fp8(L->w_in, L->rows, h, w_in8, s_in, nullptr);
-  if (e == cudaSuccess) e = quantize_tiled_weights_fp8(L->w_out, h, L->vd, w_out8, s_out, nullptr);
+  if (e == cudaSuccess) e = quantize_tiled_weights_fp8(L->w_out, h, L->vd, w_out8, s_out, nullptr, L->out_amax);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     for (void* p : {static_cast<void*>(w_in8), static_cast<void*>(w_out8), static_cast<void*>(s_in),
@@ -466,6 +484,7 @@ extern "C" gdn_status gdn_layer_set_weight_format(gdn_layer* L, int32_t format) 
   L->w_out8 = w_out8;
   L->s_in = s_in;
   L->s_out = s_out;
+  L->wformat = format;
   return GDN_OK;
 }
 
@@ -520,12 +539,17 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   float* xs = q8 ? reinterpret_cast<float*>(xq + align256(static_cast<size_t>(B) * h)) : nullptr;
   uint8_t* yq = q8 ? reinterpret_cast<uint8_t*>(xs) + align256(static_cast<size_t>(B) * 4) : nullptr;
   float* ys = q8 ? reinterpret_cast<float*>(yq + align256(static_cast<size_t>(B) * L->vd)) : nullptr;
+  const bool w8 = L->wformat == GDN_WEIGHTS_FP8_WEIGHT_ONLY;
   if (q8) {
     GDN_CUDA(quantize_rows_fp8(x, h, B, h, xq, xs, stream));
     ep.a_tiled = L->w_in8;
     ep.row_scale = L->s_in;
     ep.col_scale = xs;
     GDN_CUDA(gemm_f8_tn(L->w_in8, xq, h, L->rows, B, h, kEpiDecodeInProj, ep, stream, true, true));
+  } else if (w8) {
+    ep.a_tiled = L->w_in8;
+    ep.row_scale = L->s_in;
+    GDN_CUDA(gemm_w8_tn(L->w_in8, x, h, L->rows, B, h, kEpiDecodeInProj, ep, stream, true, true));
   } else {
     GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
   }
@@ -567,6 +591,10 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
     eo.row_scale = L->s_out;
     eo.col_scale = ys;
     GDN_CUDA(gemm_f8_tn(L->w_out8, yq, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true));
+  } else if (w8) {
+    eo.a_tiled = L->w_out8;
+    eo.row_scale = L->s_out;
+    GDN_CUDA(gemm_w8_tn(L->w_out8, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true));
   } else {
     GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true));
   }
@@ -626,7 +654,7 @@ static gdn_status forward_rows(gdn_layer* L, const uint16_t* x, int B, int T, fl
                                uint16_t* out, gdn_comm* comm, cudaStream_t stream) {
   const int64_t n = static_cast<int64_t>(B) * T;
   const int64_t chunks = T > 1 ? static_cast<int64_t>(B) * ((T + 63) / 64) : 0;
-  const bool f8 = T == 1 && L->w_in8;
+  const bool f8 = T == 1 && L->wformat == GDN_WEIGHTS_FP8_E4M3;
   gdn_status st = ensure_workspace(L, n, chunks, stream, f8);
   if (st != GDN_OK) return st;
   const int h = L->dims.hidden;

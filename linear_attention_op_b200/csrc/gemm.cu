@@ -141,9 +141,18 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
 __device__ __forceinline__ void apply_scales(const GemmEpiArgs& ep, int m, int n0, int M, int N, float (&v)[16]) {
   if (!ep.row_scale || m >= M) return;
   const float rs = ep.row_scale[m];
+  if (!ep.col_scale) {  // weight-only quantisation: the activations are bf16
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= rs;
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] *= rs * (n0 + j < N ? ep.col_scale[n0 + j] : 0.f);
 }
+
+template <int BN, int EPI>
+__device__ __forceinline__ void tn_epilogue(uint32_t tmem, uint8_t* smem, const GemmEpiArgs& ep, int m_tile, int n_tile,
+                                            int M, int N, int ksplit, int split, int warp, int lane, uint64_t* accum);
 
 // One CTA of the tcgen05 GEMM.  F8: A and B are fp8 e4m3 (kind::f8f6f4, 32-deep MMAs) and a 128-byte
 // stage row holds 128 K elements instead of 64; everything else (stage bytes, swizzle, pipeline) is the
@@ -272,6 +281,18 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap& tmA, const CUten
     __syncwarp();
   }
 
+  tn_epilogue<BN, EPI>(tmem, smem, ep, m_tile, n_tile, M, N, ksplit, split, warp, lane, accum);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// The epilogue of one 128 x BN tile (or of the tile's share after the split-K reduction); warps 2..5 own the
+// accumulator's TMEM lane quarters; every warp takes part in the split-K cluster barriers.  `smem` (the idle
+// stage ring) parks the partial tile of a split.
+template <int BN, int EPI>
+__device__ __forceinline__ void tn_epilogue(uint32_t tmem, uint8_t* smem, const GemmEpiArgs& ep, int m_tile, int n_tile,
+                                            int M, int N, int ksplit, int split, int warp, int lane, uint64_t* accum) {
   const int q = warp & 3;          // TMEM lane quarter this warp may access
   const int r = q * 32 + lane;     // row inside the tile
   const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
@@ -343,9 +364,6 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap& tmA, const CUten
     __syncwarp();
     cluster_sync();  // every slice keeps its shared memory until all have read it
   }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
 template <int BN, int STAGES, int EPI>
@@ -639,6 +657,253 @@ cudaError_t gemm_f8_tn(const void* A_tiled, const void* B, int64_t ldb, int M, i
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Weight-only fp8 decode projections: e4m3 weights x bf16 activations
+// ---------------------------------------------------------------------------------------------
+// The weights stream as e4m3 (half the bytes of bf16) in the fp8 streaming layout (16 KB blocks of 128
+// rows x 128 K, 128B swizzle); the activations stay bf16.  The tensor cores take bf16 x bf16 (kind::f16
+// wants both operands of one type), so each weight stage is widened to bf16 in shared memory first -- by
+// the epilogue warps, idle until the accumulator is ready -- into one of two 32 KB buffers (two 128 x 64
+// SW128 tiles), exactly (every e4m3 value is a bf16 value); the per-row power-of-two scale is applied in the
+// epilogue.  Pipeline per 128-K block i: warp 0 loads stage i % S (e4m3 A + bf16 B); warps 2..5 wait for it
+// and for conversion buffer i % 2 to be free, widen A into it and arrive; warp 1 issues the 8 MMAs and
+// commits both the stage and the buffer back.
+template <int BN, int STAGES>
+struct W8Cfg {
+  static constexpr int kABytes = 16384;             // e4m3 [128 rows][128 K]
+  static constexpr int kBTile = BN * kBK * 2;       // bf16 [BN rows][64 K], SW128
+  static constexpr int kStageBytes = kABytes + 2 * kBTile;
+  static constexpr int kConvOff = STAGES * kStageBytes;
+  static constexpr int kBarOffset = kConvOff + 2 * 32768;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static_assert(kSmemBytes <= 227 * 1024, "weight-only fp8 GEMM shared memory");
+  static_assert(BN * kBM * 4 <= STAGES * kStageBytes, "split-K partial tile must fit in the stage ring");
+  static_assert(kStageBytes % 1024 == 0 && kBTile % 1024 == 0, "SW128 tiles need 1024-byte alignment");
+};
+
+// 16 e4m3 values (one 16-byte chunk) -> 16 bf16 values (two 16-byte chunks), exactly.
+__device__ __forceinline__ void e4m3x16_to_bf16(const uint4& q, uint4& lo, uint4& hi) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      const __nv_fp8x2_storage_t p = static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * hlf)) & 0xffffu);
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p, __NV_E4M3);
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+      const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+      o[2 * i + hlf] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+  }
+  lo = make_uint4(o[0], o[1], o[2], o[3]);
+  hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_w8_kernel(const __grid_constant__ CUtensorMap tmB, int M, int N, int K, int ksplit, int n_tiles,
+                      int group_m, int trigger_early, const uint8_t* a8, GemmEpiArgs ep) {
+  using C = W8Cfg<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* conv = smem + C::kConvOff;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* cfull = empty + STAGES;
+  uint64_t* cempty = cfull + 2;
+  uint64_t* accum = cempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  auto stage_a = [&](int st) { return smem + st * C::kStageBytes; };
+  auto stage_b = [&](int st) { return smem + st * C::kStageBytes + C::kABytes; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x / ksplit, split = blockIdx.x % ksplit;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int per_group = group_m * n_tiles;
+  const int first_m = (tile / per_group) * group_m;
+  const int gsize = min(m_tiles - first_m, group_m);
+  const int m_tile = first_m + (tile % per_group) % gsize;
+  const int n_tile = (tile % per_group) / gsize;
+  const int kblocks = K / (2 * kBK);
+  const int kb0 = static_cast<int>(static_cast<int64_t>(split) * kblocks / ksplit);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * kblocks / ksplit);
+  const int nk = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&cfull[c], 128);  // every converter thread arrives
+      mbar_init(&cempty[c], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (trigger_early) griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (elect_one()) {
+      const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
+      auto load_a = [&](int st, int kb) {
+        bulk_load_hint(stage_a(st), a8 + (static_cast<int64_t>(m_tile) * kblocks + kb) * 16384, 16384, &full[st], pol_a);
+      };
+      auto load_b = [&](int st, int kb) {
+        tma_load_2d(stage_b(st), &tmB, &full[st], kb * 2 * kBK, n_tile * BN, pol_b);
+        tma_load_2d(stage_b(st) + C::kBTile, &tmB, &full[st], kb * 2 * kBK + kBK, n_tile * BN, pol_b);
+      };
+      // the weights do not depend on the previous kernel: the first stages are requested before waiting
+      const int pre = nk < STAGES ? nk : STAGES;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+        load_a(i, kb0 + i);
+      }
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) load_b(i, kb0 + i);
+      for (int i = pre; i < nk; ++i) {
+        const int st = i % STAGES;
+        if (!mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1, kErrWaitSmemEmpty)) break;
+        mbar_arrive_expect_tx(&full[st], C::kStageBytes);
+        load_a(st, kb0 + i);
+        load_b(st, kb0 + i);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_dense(1, kBM, BN);
+      for (int i = 0; i < nk; ++i) {
+        const int st = i % STAGES, c = i & 1;
+        if (!mbar_wait(&cfull[c], (i >> 1) & 1, kErrWaitTmaFull)) break;
+        if (!mbar_wait(&full[st], (i / STAGES) & 1, kErrWaitTmaFull)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const uint64_t da = sdesc_k_sw128(smem_u32(conv + c * 32768 + t * 16384));
+          const uint64_t db = sdesc_k_sw128(smem_u32(stage_b(st) + t * C::kBTile));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || t > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[st]);
+        umma_commit(&cempty[c]);
+      }
+      umma_commit(accum);
+    }
+    __syncwarp();
+  } else {
+    // widen each e4m3 stage into a bf16 buffer: thread j handles 16-byte chunks j, j + 128, ... (row
+    // chunk / 8, stored chunk position chunk % 8 = logical K chunk ^ (row % 8))
+    const int ctid = threadIdx.x - 64;
+    for (int i = 0; i < nk; ++i) {
+      const int st = i % STAGES, c = i & 1;
+      if (!mbar_wait(&full[st], (i / STAGES) & 1, kErrWaitTmaFull)) break;
+      if (!mbar_wait(&cempty[c], ((i >> 1) & 1) ^ 1, kErrWaitSmemEmpty)) break;
+      const uint8_t* a = stage_a(st);
+      uint8_t* d = conv + c * 32768;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int idx = ctid + 128 * j, row = idx >> 3, pos = idx & 7;
+        const int kc = pos ^ (row & 7);               // logical 16-wide K chunk: k = 16 kc .. 16 kc + 15
+        const uint4 q = *reinterpret_cast<const uint4*>(a + row * 128 + pos * 16);
+        uint4 lo, hi;
+        e4m3x16_to_bf16(q, lo, hi);
+        uint8_t* dt = d + (kc >> 2) * 16384 + row * 128;  // bf16 tile of k / 64, row `row`
+        const int c8 = (2 * kc) & 7;                      // logical 8-wide chunk inside the tile's row
+        *reinterpret_cast<uint4*>(dt + ((c8 ^ (row & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4*>(dt + (((c8 + 1) ^ (row & 7)) << 4)) = hi;
+      }
+      fence_proxy_async_shared();  // the widened tile is read by the tensor cores (async proxy)
+      mbar_arrive(&cfull[c]);
+    }
+  }
+  tn_epilogue<BN, EPI>(tmem, smem, ep, m_tile, n_tile, M, N, ksplit, split, warp, lane, accum);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+template <int BN, int STAGES, int EPI>
+static cudaError_t launch_w8(const CUtensorMap& tb, const void* a8, int M, int N, int K, const GemmEpiArgs& ep,
+                             bool pdl, bool trigger, cudaStream_t stream, int sms) {
+  using C = W8Cfg<BN, STAGES>;
+  auto kern = gemm_tn_w8_kernel<BN, STAGES, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + BN - 1) / BN, tiles = m_tiles * n_tiles;
+  const int kblocks = K / (2 * kBK);
+  static int cap[9] = {0};
+  int ksplit = one_wave_ksplit(kern, C::kSmemBytes, tiles, std::min(std::max(1, sms / tiles), kblocks), cap);
+  const int group_m = std::min(16, m_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * ksplit));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (ksplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = static_cast<unsigned>(ksplit);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kern, tb, M, N, K, ksplit, n_tiles, group_m, trigger ? 1 : 0,
+                            static_cast<const uint8_t*>(a8), ep);
+}
+
+template <int BN, int STAGES>
+static cudaError_t dispatch_w8(int epi, const CUtensorMap& tb, const void* a8, int M, int N, int K,
+                               const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t s, int sms) {
+  switch (epi) {
+    case kEpiStoreBF16T: return launch_w8<BN, STAGES, kEpiStoreBF16T>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
+    case kEpiDecodeInProj: return launch_w8<BN, STAGES, kEpiDecodeInProj>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t gemm_w8_tn(const void* A8_tiled, const void* B, int64_t ldb, int M, int N, int K, int epi,
+                       const GemmEpiArgs& ep, cudaStream_t stream, bool pdl, bool trigger) {
+  if (M <= 0 || N <= 0 || K <= 0 || (K % (2 * kBK)) || !A8_tiled || !B || !ep.row_scale || ep.col_scale ||
+      ep.b_tiled || (ep.residual && epi != kEpiStoreBF16T))
+    return cudaErrorInvalidValue;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int BN = N <= 16 ? 16 : (N <= 32 ? 32 : 64);
+  if (BN == 64 && ((M + kBM - 1) / kBM) * ((N + 63) / 64) > sms) BN = 128;  // wide batches: one wave
+  CUtensorMap tb;
+  std::memset(&tb, 0, sizeof(tb));
+  cudaError_t e = make_tmap(&tb, B, N, K, ldb, BN);
+  if (e != cudaSuccess) return e;
+  switch (BN) {
+    case 16: return dispatch_w8<16, 5>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
+    case 32: return dispatch_w8<32, 5>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
+    case 64: return dispatch_w8<64, 5>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
+    default: return dispatch_w8<128, 3>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
+  }
+}
+
 // The smallest power of two 2^e with amax / 2^e <= 448 (e4m3's largest finite value), from the bits of
 // amax / 448: that value itself when it is a power of two, else the next power up; 1 for an all-zero row.
 __device__ __forceinline__ float e4m3_scale(float amax) {
@@ -690,7 +955,8 @@ __device__ __forceinline__ void unpack8_bf16(const uint4& v, float inv, float (&
 
 // One warp per (padded) weight row: lane l handles 16-byte chunk l % 8 of bf16 blocks kb = l / 8, + 4, ...
 __global__ void quantize_tiled_weights_kernel(uint8_t* __restrict__ w16, int rows, int cols, int prow_total,
-                                              uint8_t* __restrict__ w8, float* __restrict__ scale) {
+                                              uint8_t* __restrict__ w8, float* __restrict__ scale,
+                                              const float* __restrict__ row_amax) {
   const int row = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= prow_total) return;
@@ -703,6 +969,7 @@ __global__ void quantize_tiled_weights_kernel(uint8_t* __restrict__ w16, int row
   for (int kb = lane >> 3; kb < kbt16; kb += 4) amax = fmaxf(amax, amax8_bf16(*reinterpret_cast<const uint4*>(src(kb))));
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if (row_amax) amax = row < rows ? row_amax[row] : 0.f;  // the whole row's maximum (a column shard's rows)
   const float s = e4m3_scale(amax), inv = 1.f / s;
   if (lane == 0 && row < rows) scale[row] = s;
   for (int kb = lane >> 3; kb < kbt16; kb += 4) {
@@ -720,12 +987,34 @@ __global__ void quantize_tiled_weights_kernel(uint8_t* __restrict__ w16, int row
 }
 
 cudaError_t quantize_tiled_weights_fp8(void* w_tiled, int rows, int cols, void* w8, float* scale,
-                                       cudaStream_t stream) {
+                                       cudaStream_t stream, const float* row_amax) {
   if (rows <= 0 || cols <= 0 || (cols % (2 * kBK)) || !w_tiled || !w8 || !scale) return cudaErrorInvalidValue;
   const int64_t prows = static_cast<int64_t>(tiled_weight_bytes(rows, cols) / 16384) / (cols / kBK) * kBM;
   count_launch();
   quantize_tiled_weights_kernel<<<static_cast<unsigned>((prows * 32 + 255) / 256), 256, 0, stream>>>(
-      static_cast<uint8_t*>(w_tiled), rows, cols, static_cast<int>(prows), static_cast<uint8_t*>(w8), scale);
+      static_cast<uint8_t*>(w_tiled), rows, cols, static_cast<int>(prows), static_cast<uint8_t*>(w8), scale, row_amax);
+  return cudaGetLastError();
+}
+
+// One warp per row of a row-major bf16 matrix: out[row] = max |src[row][:]|.
+__global__ void row_amax_kernel(const uint16_t* __restrict__ src, int64_t ld, int rows, int cols, float* __restrict__ out) {
+  const int row = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* r = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row) * ld);
+  float m = 0.f;
+  for (int i = lane; i < cols / 8; i += 32) m = fmaxf(m, amax8_bf16(r[i]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) out[row] = m;
+}
+
+cudaError_t row_amax_bf16(const void* src, int64_t ld, int rows, int cols, float* out, cudaStream_t stream) {
+  if (!src || !out || rows <= 0 || cols <= 0 || (cols & 7) || (ld & 7) || (reinterpret_cast<uintptr_t>(src) & 15))
+    return cudaErrorInvalidValue;
+  count_launch();
+  row_amax_kernel<<<static_cast<unsigned>((static_cast<int64_t>(rows) * 32 + 255) / 256), 256, 0, stream>>>(
+      static_cast<const uint16_t*>(src), ld, rows, cols, out);
   return cudaGetLastError();
 }
 

@@ -100,11 +100,21 @@ cudaError_t tile_weights_bf16(const void* src, int64_t ld, int rows, int cols, v
 //   gemm_f8_tn: gemm_bf16_tn's weight-streaming path with A = w8 (pre-tiled e4m3, ep.a_tiled == A) and
 //     B = xq [N, K] (row stride ldb bytes), ep.row_scale / ep.col_scale set; epi kEpiStoreBF16T or
 //     kEpiDecodeInProj.
+//   row_amax (optional): use these row maxima instead of the tiled rows' own (the rows of a column shard
+//     then get the scales of the whole rows, so every shard quantises as the unsharded matrix does).
 cudaError_t quantize_tiled_weights_fp8(void* w_tiled, int rows, int cols, void* w8, float* scale,
-                                       cudaStream_t stream);
+                                       cudaStream_t stream, const float* row_amax = nullptr);
+// out[r] = max |src[r][:]| of a row-major bf16 matrix (row stride ld elements, cols % 8 == 0).
+cudaError_t row_amax_bf16(const void* src, int64_t ld, int rows, int cols, float* out, cudaStream_t stream);
 cudaError_t quantize_rows_fp8(const void* x, int64_t ld, int rows, int cols, void* xq, float* xs,
                               cudaStream_t stream);
 cudaError_t gemm_f8_tn(const void* A_tiled, const void* B, int64_t ldb, int M, int N, int K, int epi,
+                       const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false, bool trigger = false);
+// Weight-only fp8: A8_tiled = e4m3 weights in the fp8 streaming layout (quantize_tiled_weights_fp8), B = bf16
+// activations [N, K] (row stride ldb elements), K % 128 == 0, ep.row_scale = the weights' row scales and
+// ep.col_scale null; the e4m3 stages are widened to bf16 in shared memory and multiplied on the bf16 tensor
+// cores.  epi kEpiStoreBF16T (optionally with ep.residual) or kEpiDecodeInProj.
+cudaError_t gemm_w8_tn(const void* A8_tiled, const void* B, int64_t ldb, int M, int N, int K, int epi,
                        const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false, bool trigger = false);
 
 // Number of kernel launches issued by this library since load (for the benchmark's launch count).

@@ -27,8 +27,10 @@ from ._lib import Dims, LayerInfo, MlpWeights, Weights, call
 HEAD_DIM = 128
 
 
-# The reference's weight_dtype (ttnn.bfloat16 / bfloat8_b) -> gdn_layer_set_weight_format's formats.
-WEIGHT_FORMATS = {"bf16": 0, "fp8": 1}
+# The reference's weight_dtype (ttnn.bfloat16 / bfloat8_b) -> gdn_layer_set_weight_format's formats:
+# "fp8" = e4m3 weights with bf16 activations (the reference's weight-only semantics, any tp_size);
+# "fp8_w8a8" = e4m3 weights and per-token e4m3 decode activations (tp_size 1).
+WEIGHT_FORMATS = {"bf16": 0, "fp8_w8a8": 1, "fp8": 2}
 
 
 def _stream_handle(stream: torch.cuda.Stream | None = None) -> ctypes.c_void_p:
@@ -161,9 +163,10 @@ class Qwen35GatedDeltaNet:
     (any device/dtype) returns ``[B, T, hidden]`` on x's device in x's dtype; T == 1 is a decode step,
     T > 1 a chunked prefill.  ``tp_rank``/``tp_size``/``comm`` shard the heads over GPUs (one NCCL
     all-reduce per call); with ``tp_size > 1`` and ``comm=None`` the call returns this rank's partial sum.
-    ``weight_dtype="fp8"`` (the reference's ``weight_dtype=ttnn.bfloat8_b`` mode) quantises the projection
-    weights to e4m3 with per-row power-of-two scales: decode steps stream half the weight bytes (their
-    activations are quantised per token the same way), prefill uses the dequantised weights.
+    ``weight_dtype="fp8"`` (the reference's ``weight_dtype=ttnn.bfloat8_b`` mode: weights quantised, activations
+    not) quantises the projection weights to e4m3 with per-row power-of-two scales: decode steps stream half
+    the weight bytes, prefill uses the dequantised weights; it works head-parallel too.
+    ``weight_dtype="fp8_w8a8"`` also quantises the decode activations per token (e4m3 x e4m3 GEMMs, one GPU).
     """
 
     def __init__(self, hf_layer=None, batch: int = 1, *, weights=None, device=None, tp_rank: int = 0,
