@@ -143,7 +143,7 @@ __device__ __forceinline__ void apply_scales(const GemmEpiArgs& ep, int m, int n
   const float rs = ep.row_scale[m];
   if (!ep.col_scale) {  // weight-only quantisation: the activations are bf16
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] *= rs;
+    for (int j = 0; j < 16; ++j) v[j] = (v[j] * ep.acc_scale) * rs;
     return;
   }
 #pragma unroll
@@ -296,7 +296,7 @@ __device__ __forceinline__ void tn_epilogue(uint32_t tmem, uint8_t* smem, const 
   const int q = warp & 3;          // TMEM lane quarter this warp may access
   const int r = q * 32 + lane;     // row inside the tile
   const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16);
-  const bool epi_warp = warp >= 2;
+  const bool epi_warp = warp >= 2 && warp < 6;
   GemmEpiArgs eo = ep;
   if (epi_warp) {
     griddep_wait();  // the epilogue writes buffers the previous kernel may still read
@@ -421,10 +421,10 @@ static cudaError_t make_tmap(CUtensorMap* map, const void* ptr, int64_t rows, in
 // How many clusters of `ks` CTAs of this kernel can be resident at once (the unit a split-K launch is
 // scheduled in: a cluster must fit inside one GPC, so CTA-level occupancy overestimates it).
 template <class Kern>
-static int cluster_capacity(Kern kern, int ks, int smem) {
+static int cluster_capacity(Kern kern, int ks, int smem, int threads = kGemmThreads) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(ks * 64));
-  cfg.blockDim = dim3(kGemmThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -439,7 +439,7 @@ static int cluster_capacity(Kern kern, int ks, int smem) {
     int blocks = 0, dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, kGemmThreads, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, threads, smem);
     n = std::max(1, blocks * sms / ks);
   }
   return n;
@@ -466,9 +466,9 @@ static int choose_ksplit(Kern kern, int smem, int tiles, int kblocks, int (&cap)
 // Weight-streaming GEMMs: the largest split in [1, kmax] whose clusters all fit on the device at once (one
 // wave), else 1.
 template <class Kern>
-static int one_wave_ksplit(Kern kern, int smem, int tiles, int kmax, int (&cap)[9]) {
+static int one_wave_ksplit(Kern kern, int smem, int tiles, int kmax, int (&cap)[9], int threads = kGemmThreads) {
   for (int ks = std::min(kmax, 8); ks > 1; --ks) {
-    if (!cap[ks]) cap[ks] = cluster_capacity(kern, ks, smem);
+    if (!cap[ks]) cap[ks] = cluster_capacity(kern, ks, smem, threads);
     if (tiles <= cap[ks]) return ks;
   }
   return 1;
@@ -668,13 +668,14 @@ cudaError_t gemm_f8_tn(const void* A_tiled, const void* B, int64_t ldb, int M, i
 // epilogue.  Pipeline per 128-K block i: warp 0 loads stage i % S (e4m3 A + bf16 B); warps 2..5 wait for it
 // and for conversion buffer i % 2 to be free, widen A into it and arrive; warp 1 issues the 8 MMAs and
 // commits both the stage and the buffer back.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int NCONV = 2>
 struct W8Cfg {
+  static constexpr int kConv = NCONV;                 // bf16 widening buffers
   static constexpr int kABytes = 16384;             // e4m3 [128 rows][128 K]
   static constexpr int kBTile = BN * kBK * 2;       // bf16 [BN rows][64 K], SW128
   static constexpr int kStageBytes = kABytes + 2 * kBTile;
   static constexpr int kConvOff = STAGES * kStageBytes;
-  static constexpr int kBarOffset = kConvOff + 2 * 32768;
+  static constexpr int kBarOffset = kConvOff + NCONV * 32768;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static_assert(kSmemBytes <= 227 * 1024, "weight-only fp8 GEMM shared memory");
@@ -682,38 +683,39 @@ struct W8Cfg {
   static_assert(kStageBytes % 1024 == 0 && kBTile % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 };
 
-// 16 e4m3 values (one 16-byte chunk) -> 16 bf16 values (two 16-byte chunks), exactly.
+// 16 e4m3 values (one 16-byte chunk) -> the 16 bf16 values e4m3 * 2^-120 (two 16-byte chunks), exactly, by
+// placing the bits: e4m3 s.eeee.mmm -> bf16 s.0000eeee.mmm0000.  A normal e4m3 (eeee > 0) becomes the normal
+// bf16 2^(eeee - 127) (1 + m/8) = value * 2^-120, an e4m3 subnormal (eeee = 0) the bf16 subnormal
+// 2^-126 (m/8) = value * 2^-120, and zero stays zero; the quantiser never writes NaN.  Integer ALU work only
+// (byte permute, shift, mask), where the conversion instructions through f16 and f32 took four per pair of
+// values.  The epilogue multiplies the accumulator by 2^120 (GemmEpiArgs.acc_scale).
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2_scaled(uint32_t w, uint32_t sel) {
+  uint32_t u;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(u) : "r"(w), "r"(sel));  // byte b_lo -> bits 8..15, b_hi -> 24..31
+  return (u & 0x80008000u) | ((u >> 4) & 0x07F007F0u);            // sign stays; magnitude moves to bits 4..10
+}
 __device__ __forceinline__ void e4m3x16_to_bf16(const uint4& q, uint4& lo, uint4& hi) {
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-  uint32_t o[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int hlf = 0; hlf < 2; ++hlf) {
-      const __nv_fp8x2_storage_t p = static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * hlf)) & 0xffffu);
-      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p, __NV_E4M3);
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-      const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
-      o[2 * i + hlf] = *reinterpret_cast<const uint32_t*>(&b);
-    }
-  }
-  lo = make_uint4(o[0], o[1], o[2], o[3]);
-  hi = make_uint4(o[4], o[5], o[6], o[7]);
+  lo = make_uint4(e4m3x2_to_bf16x2_scaled(q.x, 0x1504u), e4m3x2_to_bf16x2_scaled(q.x, 0x3524u),
+                  e4m3x2_to_bf16x2_scaled(q.y, 0x1504u), e4m3x2_to_bf16x2_scaled(q.y, 0x3524u));
+  hi = make_uint4(e4m3x2_to_bf16x2_scaled(q.z, 0x1504u), e4m3x2_to_bf16x2_scaled(q.z, 0x3524u),
+                  e4m3x2_to_bf16x2_scaled(q.w, 0x1504u), e4m3x2_to_bf16x2_scaled(q.w, 0x3524u));
 }
 
-template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+constexpr int kW8Threads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 widen the weights (2..5 then the epilogue)
+
+template <int BN, int STAGES, int NCONV, int EPI>
+__global__ void __launch_bounds__(kW8Threads, 1)
     gemm_tn_w8_kernel(const __grid_constant__ CUtensorMap tmB, int M, int N, int K, int ksplit, int n_tiles,
                       int group_m, int trigger_early, const uint8_t* a8, GemmEpiArgs ep) {
-  using C = W8Cfg<BN, STAGES>;
+  using C = W8Cfg<BN, STAGES, NCONV>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* conv = smem + C::kConvOff;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
   uint64_t* empty = full + STAGES;
   uint64_t* cfull = empty + STAGES;
-  uint64_t* cempty = cfull + 2;
-  uint64_t* accum = cempty + 2;
+  uint64_t* cempty = cfull + C::kConv;
+  uint64_t* accum = cempty + C::kConv;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   auto stage_a = [&](int st) { return smem + st * C::kStageBytes; };
   auto stage_b = [&](int st) { return smem + st * C::kStageBytes + C::kABytes; };
@@ -736,8 +738,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], 1);
     }
-    for (int c = 0; c < 2; ++c) {
-      mbar_init(&cfull[c], 128);  // every converter thread arrives
+    for (int c = 0; c < C::kConv; ++c) {
+      mbar_init(&cfull[c], (kW8Threads - 64) / 32);  // one arrival per converter warp
       mbar_init(&cempty[c], 1);
     }
     mbar_init(accum, 1);
@@ -785,8 +787,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_dense(1, kBM, BN);
       for (int i = 0; i < nk; ++i) {
-        const int st = i % STAGES, c = i & 1;
-        if (!mbar_wait(&cfull[c], (i >> 1) & 1, kErrWaitTmaFull)) break;
+        const int st = i % STAGES, c = i % C::kConv;
+        if (!mbar_wait(&cfull[c], (i / C::kConv) & 1, kErrWaitTmaFull)) break;
         if (!mbar_wait(&full[st], (i / STAGES) & 1, kErrWaitTmaFull)) break;
         tc_fence_after();
 #pragma unroll
@@ -803,29 +805,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
   } else {
-    // widen each e4m3 stage into a bf16 buffer: thread j handles 16-byte chunks j, j + 128, ... (row
-    // chunk / 8, stored chunk position chunk % 8 = logical K chunk ^ (row % 8))
+    // Widen each e4m3 stage into a bf16 buffer.  Thread j handles 16-byte chunks j, j + 256, j + 512, j + 768:
+    // chunk idx is row idx / 8, stored position idx % 8 = logical 16-wide K chunk kc ^ (row % 8), so the
+    // row's swizzle phase -- and with it every address offset -- is the same for all four.  The two bf16
+    // halves of a chunk go to tile kc / 4 at 8-wide positions 2 kc % 8 and + 1; lanes with kc < 4 store
+    // their low half first and the others their high half, so the 8 lanes of each store phase hit 8
+    // distinct 16-byte bank groups.
     const int ctid = threadIdx.x - 64;
+    const int pos = ctid & 7, row0 = ctid >> 3, sw = row0 & 7;  // row0 + 32 j keeps row % 8 == sw
+    const int kc = pos ^ sw, c8 = (2 * kc) & 7;
+    const uint32_t off_first = (kc >> 2) * 16384 + ((((kc < 4) ? c8 : c8 + 1) ^ sw) << 4);
+    const uint32_t off_second = (kc >> 2) * 16384 + ((((kc < 4) ? c8 + 1 : c8) ^ sw) << 4);
     for (int i = 0; i < nk; ++i) {
-      const int st = i % STAGES, c = i & 1;
+      const int st = i % STAGES, c = i % C::kConv;
       if (!mbar_wait(&full[st], (i / STAGES) & 1, kErrWaitTmaFull)) break;
-      if (!mbar_wait(&cempty[c], ((i >> 1) & 1) ^ 1, kErrWaitSmemEmpty)) break;
-      const uint8_t* a = stage_a(st);
-      uint8_t* d = conv + c * 32768;
+      if (!mbar_wait(&cempty[c], ((i / C::kConv) & 1) ^ 1, kErrWaitSmemEmpty)) break;
+      const uint8_t* a = stage_a(st) + row0 * 128 + pos * 16;
+      uint8_t* d = conv + c * 32768 + row0 * 128;
+      uint4 q[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int idx = ctid + 128 * j, row = idx >> 3, pos = idx & 7;
-        const int kc = pos ^ (row & 7);               // logical 16-wide K chunk: k = 16 kc .. 16 kc + 15
-        const uint4 q = *reinterpret_cast<const uint4*>(a + row * 128 + pos * 16);
+      for (int j = 0; j < 4; ++j) q[j] = *reinterpret_cast<const uint4*>(a + j * 32 * 128);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
         uint4 lo, hi;
-        e4m3x16_to_bf16(q, lo, hi);
-        uint8_t* dt = d + (kc >> 2) * 16384 + row * 128;  // bf16 tile of k / 64, row `row`
-        const int c8 = (2 * kc) & 7;                      // logical 8-wide chunk inside the tile's row
-        *reinterpret_cast<uint4*>(dt + ((c8 ^ (row & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4*>(dt + (((c8 + 1) ^ (row & 7)) << 4)) = hi;
+        e4m3x16_to_bf16(q[j], lo, hi);
+        *reinterpret_cast<uint4*>(d + j * 32 * 128 + off_first) = kc < 4 ? lo : hi;
+        *reinterpret_cast<uint4*>(d + j * 32 * 128 + off_second) = kc < 4 ? hi : lo;
       }
       fence_proxy_async_shared();  // the widened tile is read by the tensor cores (async proxy)
-      mbar_arrive(&cfull[c]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&cfull[c]);
     }
   }
   tn_epilogue<BN, EPI>(tmem, smem, ep, m_tile, n_tile, M, N, ksplit, split, warp, lane, accum);
@@ -834,21 +843,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int NCONV, int EPI>
 static cudaError_t launch_w8(const CUtensorMap& tb, const void* a8, int M, int N, int K, const GemmEpiArgs& ep,
                              bool pdl, bool trigger, cudaStream_t stream, int sms) {
-  using C = W8Cfg<BN, STAGES>;
-  auto kern = gemm_tn_w8_kernel<BN, STAGES, EPI>;
+  using C = W8Cfg<BN, STAGES, NCONV>;
+  auto kern = gemm_tn_w8_kernel<BN, STAGES, NCONV, EPI>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + BN - 1) / BN, tiles = m_tiles * n_tiles;
   const int kblocks = K / (2 * kBK);
   static int cap[9] = {0};
-  int ksplit = one_wave_ksplit(kern, C::kSmemBytes, tiles, std::min(std::max(1, sms / tiles), kblocks), cap);
+  int ksplit = one_wave_ksplit(kern, C::kSmemBytes, tiles, std::min(std::max(1, sms / tiles), kblocks), cap,
+                               kW8Threads);
   const int group_m = std::min(16, m_tiles);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(tiles * ksplit));
-  cfg.blockDim = dim3(kGemmThreads);
+  cfg.blockDim = dim3(kW8Threads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -872,12 +882,13 @@ static cudaError_t launch_w8(const CUtensorMap& tb, const void* a8, int M, int N
                             static_cast<const uint8_t*>(a8), ep);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int NCONV>
 static cudaError_t dispatch_w8(int epi, const CUtensorMap& tb, const void* a8, int M, int N, int K,
                                const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t s, int sms) {
   switch (epi) {
-    case kEpiStoreBF16T: return launch_w8<BN, STAGES, kEpiStoreBF16T>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
-    case kEpiDecodeInProj: return launch_w8<BN, STAGES, kEpiDecodeInProj>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
+    case kEpiStoreBF16T: return launch_w8<BN, STAGES, NCONV, kEpiStoreBF16T>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
+    case kEpiDecodeInProj:
+      return launch_w8<BN, STAGES, NCONV, kEpiDecodeInProj>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -896,11 +907,13 @@ cudaError_t gemm_w8_tn(const void* A8_tiled, const void* B, int64_t ldb, int M, 
   std::memset(&tb, 0, sizeof(tb));
   cudaError_t e = make_tmap(&tb, B, N, K, ldb, BN);
   if (e != cudaSuccess) return e;
+  GemmEpiArgs ew = ep;
+  ew.acc_scale = 0x1p120f;  // the widened weights are e4m3 * 2^-120
   switch (BN) {
-    case 16: return dispatch_w8<16, 5>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
-    case 32: return dispatch_w8<32, 5>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
-    case 64: return dispatch_w8<64, 5>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
-    default: return dispatch_w8<128, 3>(epi, tb, A8_tiled, M, N, K, ep, pdl, trigger, stream, sms);
+    case 16: return dispatch_w8<16, 5, 2>(epi, tb, A8_tiled, M, N, K, ew, pdl, trigger, stream, sms);
+    case 32: return dispatch_w8<32, 5, 2>(epi, tb, A8_tiled, M, N, K, ew, pdl, trigger, stream, sms);
+    case 64: return dispatch_w8<64, 5, 2>(epi, tb, A8_tiled, M, N, K, ew, pdl, trigger, stream, sms);
+    default: return dispatch_w8<128, 3, 2>(epi, tb, A8_tiled, M, N, K, ew, pdl, trigger, stream, sms);
   }
 }
 

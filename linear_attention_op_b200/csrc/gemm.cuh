@@ -50,6 +50,8 @@ struct GemmEpiArgs {
   // gemm_f8_tn only: acc[m][n] is multiplied by row_scale[m] * col_scale[n] (the operands' e4m3 scales)
   const float* row_scale = nullptr;
   const float* col_scale = nullptr;
+  // with row_scale and no col_scale (weight-only fp8): acc * acc_scale * row_scale[m]
+  float acc_scale = 1.0f;
   // kEpiStoreBF16T (gemm_bf16_tn) and kEpiStoreBF16 (gemm_bf16_persistent): when set, the stored value is
   // bf16(acc + residual) with residual bf16 in the output's layout, row stride res_ld (may alias `out`:
   // every element is read and then written by the same thread).
