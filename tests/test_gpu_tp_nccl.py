@@ -1,6 +1,7 @@
-"""Head-parallel layer over 2 (or 4) GPUs with the library's communicator (NVLink all-reduce for small
+"""Head-parallel layer over 2, 4 or 8 GPUs with the library's communicator (NVLink all-reduce for small
 outputs, NCCL above 8 MiB): every rank gets the full, all-reduced output, and the ranks' states tile the
-single-GPU state.  Skipped with fewer GPUs."""
+single-GPU state -- for bf16 weights, for weight-only fp8 (whole-row out_proj scales) and for the decoder
+layer around the mixer (two all-reduces per call).  Skipped with fewer GPUs."""
 import os
 import socket
 
@@ -47,12 +48,41 @@ def _worker(rank, world, port, q):
         # an output above the NVLink all-reduce's 8 MiB slot (4104 x 1024 bf16) takes the NCCL path
         xl = O.make_hidden(1, 4104, 1024, seed=9)
         yl = Qwen35GatedDeltaNet(weights=w, batch=1, tp_rank=rank, tp_size=world, comm=comm)(xl)
+        # weight-only fp8: every shard quantises out_proj with the whole rows' scales, so the all-reduced
+        # decode output matches the single-GPU quantised layer
+        wq = O.fp8_weights(w)
+        want_q, _, _ = O.layer_forward(wq, xd, s_want, c_want, mode="recurrent")
+        lq = Qwen35GatedDeltaNet(weights=w, batch=2, tp_rank=rank, tp_size=world, comm=comm, weight_dtype="fp8")
+        hvl = 32 // world
+        lq.set_state(rec_state=s_want[:, rank * hvl:(rank + 1) * hvl])
+        conv_idx = torch.cat([torch.arange(rank * 128 * (16 // world), (rank + 1) * 128 * (16 // world)),
+                              2048 + torch.arange(rank * 128 * (16 // world), (rank + 1) * 128 * (16 // world)),
+                              4096 + torch.arange(rank * 128 * hvl, (rank + 1) * 128 * hvl)])
+        lq.set_state(conv_state=c_want[:, :, conv_idx])
+        yq = lq(xd)
+        # the decoder layer around the mixer: two all-reduces per call (mixer output, MLP output)
+        from linear_attention_op_b200 import DecoderMlpWeights, Qwen35DecoderLayer
+        gen = torch.Generator().manual_seed(90)
+        rn = lambda *sz: O.bf16_round(torch.randn(*sz, generator=gen) * 0.02)
+        dw = O.DecoderWeights(gdn=w, input_norm_w=torch.rand(1024, generator=gen) - 0.5,
+                              post_norm_w=torch.rand(1024, generator=gen) - 0.5, w_gate=rn(2048, 1024),
+                              w_up=rn(2048, 1024), w_down=rn(1024, 2048))
+        want_dp, sd, cd = O.decoder_layer_forward(dw, x, mode="chunk", bf16_acts=True)
+        want_dd, sd, cd = O.decoder_layer_forward(dw, xd, sd, cd, mode="recurrent", bf16_acts=True)
+        dec = Qwen35DecoderLayer(batch=2, mixer_weights=w, comm=comm, tp_rank=rank, tp_size=world,
+                                 mlp_weights=DecoderMlpWeights(dw.input_norm_w, dw.post_norm_w, dw.w_gate, dw.w_up,
+                                                               dw.w_down))
+        ydp = dec(x)
+        ydd = dec(xd)
         err = device_error()
         hv = 32 // world
         res = dict(
             out=O.max_abs_rel(y.float(), want), state=O.max_abs_rel(s_loc, s_want[:, rank * hv:(rank + 1) * hv]),
             out_dec=O.max_abs_rel(yd.float(), want_d),
-            state_dec=O.max_abs_rel(s_loc_d, s_want_d[:, rank * hv:(rank + 1) * hv]), err=err)
+            state_dec=O.max_abs_rel(s_loc_d, s_want_d[:, rank * hv:(rank + 1) * hv]), err=err,
+            out_fp8=O.max_abs_rel(yq.float(), want_q), dec_pre=O.max_abs_rel(ydp.float(), want_dp),
+            dec_dec=O.max_abs_rel(ydd.float(), want_dd),
+            dec_state=O.max_abs_rel(dec.get_recurrent_state(), sd[:, rank * hv:(rank + 1) * hv]))
         if rank == 0:
             res["out_large"] = O.max_abs_rel(yl.float(), O.layer_forward(w, xl, mode="chunk")[0])
         comm.close()
@@ -86,5 +116,7 @@ def test_tensor_parallel_layer_nccl(world):
         assert r["err"] == 0
         assert r["out"] <= 2e-2 and r["out_dec"] <= 2e-2, r
         assert r["state"] <= 1e-3 and r["state_dec"] <= 1e-3, r
+        assert r["out_fp8"] <= 2e-2, r
+        assert r["dec_pre"] <= 2e-2 and r["dec_dec"] <= 2e-2 and r["dec_state"] <= 1e-3, r
         if rank == 0:
             assert r["out_large"] <= 2e-2, r
