@@ -545,9 +545,9 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
   else if (N <= 128) BN = 128;
   else BN = 256;
   if (ep.b_tiled && BN < 128) BN = 128;  // a tiled B operand comes in whole 128-row blocks
-  // Weight-streaming (decode) GEMMs keep N tiles of at most 64 tokens: wider batches become more N tiles
-  // that read the same weight blocks at about the same time (one HBM read, the rest L2 hits), instead of
-  // fewer, split-K CTAs.
+  // Weight-streaming (decode) GEMMs start from N tiles of at most 64 tokens (the tiles of a wide batch read
+  // the same weight blocks at about the same time: one HBM read, the rest L2 hits); batches wider than 64
+  // tokens may take 128- or 256-token tiles below.
   if (ep.a_tiled && BN > 64) BN = 64;
   if ((ep.a_tiled && A != ep.a_tiled) || (ep.b_tiled && B != ep.b_tiled)) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
@@ -566,6 +566,34 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (N > 64 && ksplit <= 0) {
+      // Wide batches (tensor-parallel decode: 64 sequences per GPU, so 128 .. 512 token columns): every CTA
+      // streams its K range of one weight tile and of BN token rows, so per-CTA bytes ~ K / ksplit * (128 +
+      // BN).  Wider token tiles mean fewer tiles, hence a deeper split inside one wave, hence fewer bytes per
+      // CTA: pick the BN in {64, 128, 256} that minimises them (64 keeps its two-CTAs-per-SM path).
+      const int m_tiles = (M + kBM - 1) / kBM, kblocks = (K + kBK - 1) / kBK;
+      int best_bn = 64;
+      double best = 1e30;
+      for (int bn : {64, 128, 256}) {
+        const int t = m_tiles * ((N + bn - 1) / bn);
+        int ks;
+        if (bn == 64) ks = t > sms ? std::max(1, std::min(8, 2 * sms / t)) : std::max(1, std::min(8, sms / t));
+        else if (t <= sms) ks = std::max(1, std::min(8, sms / t));
+        else continue;
+        const double cost = static_cast<double>((kblocks + ks - 1) / ks) * (kBM + bn);
+        if (cost < best - 1e-9) {
+          best = cost;
+          best_bn = bn;
+        }
+      }
+      if (best_bn > 64) {
+        const int t = m_tiles * ((N + best_bn - 1) / best_bn);
+        const int ks = -std::max(1, std::min(8, sms / t));  // < 0: largest split that stays one wave
+        if ((e = make_tmap(&tb, B, N, K, ldb, best_bn)) != cudaSuccess) return e;
+        if (best_bn == 128) return dispatch_epi<128, 6>(epi, ta, tb, M, N, K, ks, ep, pdl, trigger, stream);
+        return dispatch_epi<256, 4>(epi, ta, tb, M, N, K, ks, ep, pdl, trigger, stream);
+      }
+    }
     const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
     const int k1 = sms / tiles;
     const bool two_per_sm = ksplit <= 0 && k1 == 0;

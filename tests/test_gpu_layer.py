@@ -219,3 +219,26 @@ def test_cuda_graph_decode_replay():
         graph.replay()
         outs.append(out.float().cpu().clone())
     check("graph replay", torch.cat(outs, 1), want, max_rel=1e-6, min_pcc=None, max_fro=None)
+
+
+def test_tp8_shards_wide_batch_decode_on_one_gpu():
+    """The eight head-parallel shards of the 9B layer at 512 sequences (64 per GPU, the 8-GPU benchmark's
+    batch) run on one GPU without the all-reduce: their decode in_proj takes 256-token tiles with split-K,
+    and the partial outputs sum to the full layer."""
+    w = O.make_weights(4096, 16, 32, seed=13)
+    B = 512
+    x = O.make_hidden(B, 1, 4096, seed=13)
+    s0 = torch.randn(B, 32, 128, 128, generator=torch.Generator().manual_seed(14)) * 0.1
+    with torch.no_grad():
+        want, s, _ = O.layer_forward(w, x, rec_state=s0, mode="recurrent")
+    total = torch.zeros(B, 1, 4096)
+    states = []
+    for r in range(8):
+        L = Qwen35GatedDeltaNet(weights=w, batch=B, tp_rank=r, tp_size=8)
+        L.set_state(rec_state=s0[:, 4 * r:4 * (r + 1)])
+        total += L(x).float()
+        states.append(L.get_recurrent_state())
+        del L
+    assert device_error() == 0
+    check("tp8 shards at B=512: sum of partials", total, want)
+    check("tp8 shards at B=512: states", torch.cat(states, 1), s, max_rel=STATE_TOL)
