@@ -298,12 +298,16 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(ChunkArgs p, ui
     // this warp's TMEM quarter of the [K; Q] K^T accumulator (re-read per head, so no registers stay
     // allocated to it through the inverse)
     float acc[64];
+    {  // both halves in flight, one wait
+      uint32_t r0[32], r1[32];
+      tmem_ld32_async(tmem + (static_cast<uint32_t>(q4 * 32) << 16), r0);
+      tmem_ld32_async(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32, r1);
+      tmem_wait_ld();
 #pragma unroll
-    for (int c16 = 0; c16 < 4; ++c16) {
-      float v[16];
-      tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 16 * c16, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[16 * c16 + i] = v[i];
+      for (int i = 0; i < 32; ++i) {
+        acc[i] = __uint_as_float(r0[i]);
+        acc[32 + i] = __uint_as_float(r1[i]);
+      }
     }
     group_sync();
     uint8_t* img = timg + ((static_cast<int64_t>(b) * p.Hv + h) * nchunks + ch) * kTImageBytes;
@@ -499,13 +503,11 @@ __device__ __forceinline__ void butterfly_step(float (&a)[32], int lane) {
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t addr, float* out) {
-  float v[16];
-  tmem_ld16(addr, v);
+  uint32_t r[32];
+  tmem_ld32_async(addr, r);
+  tmem_wait_ld();
 #pragma unroll
-  for (int i = 0; i < 16; ++i) out[i] = v[i];
-  tmem_ld16(addr + 16, v);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) out[16 + i] = v[i];
+  for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(r[i]);
 }
 
 // Write 32 consecutive k values (k0 .. k0+31, k0 a multiple of 32) of row r into a hi/lo tile pair.
@@ -749,8 +751,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     float o[32];
     {
       float av[32];
-      tmem_ld32(tmem + lane_base + kColP1 + 64 + 32 * half, o);
-      tmem_ld32(tmem + lane_base + kColAv + 32 * half, av);
+      {  // both loads in flight, one wait
+        uint32_t ro[32], ra[32];
+        tmem_ld32_async(tmem + lane_base + kColP1 + 64 + 32 * half, ro);
+        tmem_ld32_async(tmem + lane_base + kColAv + 32 * half, ra);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          o[j] = __uint_as_float(ro[j]);
+          av[j] = __uint_as_float(ra[j]);
+        }
+      }
       float a[32];
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
