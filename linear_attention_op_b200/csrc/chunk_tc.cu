@@ -640,6 +640,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ++n_mma[0];
   };
 
+  // MMA1 of chunk c + 1 is issued as soon as chunk c's state update is in shared memory, so that it runs
+  // (and its K image finishes arriving) while chunk c's output, RMSNorm and y store are computed.
+  if (tid == 0) issue_mma1(0);
   for (int ch = 0; ch < nchunks; ++ch) {
     const int t0 = ch * kC, L = min(kC, p.T - t0);
     const int64_t row0 = static_cast<int64_t>(b) * p.T + t0;
@@ -648,9 +651,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* g_beta = gt;
     const float* g_eG = gt + kC;
     const float* g_eCG = gt + 2 * kC;
-    if (tid == 0) {
-      bulk_wait_read();  // the previous chunk's y tile has left vn_h (rewritten in phase V)
-      issue_mma1(ch);
+    if (tid == 0 && ch + 1 < nchunks) {
+      // The next chunk's K image, T / A image, v rows and z rows can only be copied into shared memory once
+      // this chunk has finished with their buffers; bring them into L2 now so that those copies are short.
+      prefetch_l2(kimg_h + static_cast<int64_t>(ch + 1) * kKImageBytes, kKImageBytes);
+      prefetch_l2(timg_h + static_cast<int64_t>(ch + 1) * kTImageBytes, 3 * 8192);
+      prefetch_l2_2d(&tm_v, v_col, b * p.T + (ch + 1) * kC);
+      prefetch_l2_2d(&tm_z, z_col, b * p.T + (ch + 1) * kC);
     }
     __syncwarp();
     // V of phase R from the prefetched rows (then the buffer becomes R^T)
@@ -680,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       write_row32(rv_h, rv_l, v, 32 * half, ks);
     }
+    if (tid == 0) bulk_wait_read();  // the previous chunk's y tile has left vn_h (rewritten in phase V)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -803,6 +811,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.rstd[tid] = rsqrtf((sm.red[0][tid] + sm.red[1][tid] + sm.red[2][tid] + sm.red[3][tid]) * (1.0f / kD) + p.eps);
     if (tid == 0 && ch + 1 < nchunks) load_rows(ch + 1, &tm_z, z_col, sm.zrows, &sm.bar_z, n_z);
     __syncthreads();
+    // The next chunk's MMA1 reads only S^T (written before the barrier above) and its K image, and
+    // overwrites (K^S)^T | (Q^S)^T, which this chunk's output took from TMEM before that barrier: it runs
+    // (and its K image finishes arriving) while this chunk's y is computed and stored.
+    if (tid == 0 && ch + 1 < nchunks && !sm.abort) issue_mma1(ch + 1);
     // y = O rstd w SiLU(z): a full chunk is staged as a [64 t][128 v] bf16 tile in vn_h (free since MMA3) and
     // leaves by one TMA store; a partial last chunk is stored directly (the box would spill into the next
     // sequence's rows).
