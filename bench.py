@@ -462,10 +462,13 @@ def run_ours(args):
         result["parity"] = parity
     if args.prefill:
         result["prefill"] = run_prefill(args, layer, dev, world, pk)
-    if args.stack:
+    if args.variants or args.stack:
         del graph, layer
         graph = None
         torch.cuda.empty_cache()
+    if args.variants:
+        result.update(run_variants(args, rank, world, comm, dev, pk))
+    if args.stack:
         result["stack"] = run_stack(args, rank, world, comm, dev, pk)
     if device_error() != 0:
         raise SystemExit("device error during the benchmark")
@@ -529,6 +532,99 @@ def run_prefill(args, layer_dec, dev, world, pk):
         "recurrence_tflops": round(fl["recurrence"] / (rec_ms * 1e-3) / 1e12, 2),
         "clocks": clk.summary(),
     }
+
+
+def graph_decode_us(forward, x, out, steps: int, world: int, dev) -> float:
+    """Per-step device time (us) of `forward(x, out, stream)` replayed from a CUDA graph of 8 steps, max over
+    ranks, after an eager warm-up and one graph replay."""
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        forward(x, out, stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(8):
+            forward(x, out, stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        if world > 1:
+            graph.replay()
+        s.record(stream)
+        for _ in range(max(1, steps // 8)):
+            graph.replay()
+        e.record(stream)
+    torch.cuda.synchronize()
+    us = max_over_ranks(s.elapsed_time(e) * 1e3 / (8 * max(1, steps // 8)), world)
+    del graph
+    return us
+
+
+def run_variants(args, rank, world, comm, dev, pk):
+    """Rows f3 and f4 of the hot-path scope at the benchmark's decode batch (64 sequences per GPU, 9B
+    geometry, head-parallel over the N GPUs): the layer with weight-only fp8 weights, and the whole decoder
+    layer around the mixer (input RMSNorm, mixer, residual, post RMSNorm, SwiGLU MLP with intermediate 12288,
+    residual; two all-reduces per call with N > 1), decode from CUDA graphs and a config-3-sized prefill."""
+    from linear_attention_op_b200 import DecoderMlpWeights, Qwen35DecoderLayer, Qwen35GatedDeltaNet
+
+    B, I = DECODE_B * world, 12288
+    W = synthetic_weights(0, dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(B, 1, H, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    res = {}
+    lq = Qwen35GatedDeltaNet(weights=W, batch=B, device=dev, tp_rank=rank, tp_size=world, comm=comm, max_rows=B,
+                             weight_dtype="fp8")
+    us = graph_decode_us(lambda a, o, st: lq.forward_into(a, o, stream=st), x, out, args.steps, world, dev)
+    byt = decode_bytes(B, world, 1)["step"]
+    res["fp8_weight_only"] = {
+        "workload": f"cfg2 decode with weight-only fp8 (e4m3) projection weights, batch {B}, tp{world}",
+        "us_per_step": round(us, 2), "tokens_per_s": round(B / (us * 1e-6), 1), "step_bytes": byt,
+        "step_hbm_frac": round(byt / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4)}
+    del lq
+    rn = lambda *sz: (torch.randn(*sz, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    mlp = DecoderMlpWeights(input_norm_w=torch.rand(H, generator=g, device=dev) - 0.5,
+                            post_norm_w=torch.rand(H, generator=g, device=dev) - 0.5,
+                            w_gate=rn(I, H), w_up=rn(I, H), w_down=rn(H, I))
+    dec = Qwen35DecoderLayer(batch=B, mixer_weights=W, mlp_weights=mlp, device=dev, tp_rank=rank, tp_size=world,
+                             comm=comm, max_rows=B)
+    us = graph_decode_us(lambda a, o, st: dec.forward_into(a, o, stream=st), x, out, args.steps, world, dev)
+    byt = decode_bytes(B, world)["step"] + 3 * H * (I // world) * 2 + 4 * B * H * 2
+    entry = {"workload": f"Qwen3.5-9B linear-attention decoder layer (mixer + SwiGLU MLP, intermediate {I}), "
+                         f"batch {B} decode, tp{world}",
+             "decode_us_per_step": round(us, 2), "decode_tokens_per_s": round(B / (us * 1e-6), 1),
+             "decode_step_bytes": byt, "decode_step_hbm_frac": round(byt / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4)}
+    del dec
+    dp = Qwen35DecoderLayer(batch=PREFILL_B, mixer_weights=W, mlp_weights=mlp, device=dev, tp_rank=rank,
+                            tp_size=world, comm=comm, max_rows=PREFILL_B * PREFILL_T)
+    xp = torch.randn(PREFILL_B, PREFILL_T, H, generator=g, device=dev).to(torch.bfloat16)
+    op = torch.empty_like(xp)
+    for _ in range(2):
+        dp.forward_into(xp, op)
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dp.forward_into(xp, op)
+    s.record()
+    for _ in range(3):
+        dp.forward_into(xp, op)
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e), world) / 3
+    fl = prefill_flops(PREFILL_B, PREFILL_T, world)["step"] + 6 * PREFILL_B * PREFILL_T * H * (I // world)
+    entry.update({"prefill_workload": f"batch {PREFILL_B} x {PREFILL_T} tokens", "prefill_ms": round(ms, 3),
+                  "prefill_tokens_per_s": round(PREFILL_B * PREFILL_T / (ms * 1e-3), 1),
+                  "prefill_tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+                  "prefill_tensor_frac": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4)})
+    res["decoder"] = entry
+    del dp, xp, op
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_stack(args, rank, world, comm, dev, pk):
@@ -670,6 +766,8 @@ def main():
     ap.add_argument("--prefill-b", type=int, default=PREFILL_B)
     ap.add_argument("--prefill-t", type=int, default=PREFILL_T)
     ap.add_argument("--no-stack", dest="stack", action="store_false", help="skip the config-4 stack line")
+    ap.add_argument("--no-variants", dest="variants", action="store_false",
+                    help="skip the weight-only fp8 and decoder-layer lines")
     ap.add_argument("--stack-layers", type=int, default=24)
     ap.add_argument("--stack-prefill", type=int, default=4096)
     ap.add_argument("--stack-steps", type=int, default=512)
@@ -682,6 +780,7 @@ def main():
         args.prefill = False
     if args.only != "all":
         args.stack = False
+        args.variants = False
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
