@@ -514,9 +514,9 @@ extern "C" gdn_status gdn_layer_set_stage_events(gdn_layer* L, void* const* even
   return GDN_OK;
 }
 
-// One decode step (T = 1): in_proj (weights as the 128-row operand, gating fused into the epilogue) ->
-// conv + conv-state roll + gated delta rule + gated RMSNorm (decode_step_kernel, which loads the state
-// and the conv history while the GEMM runs) -> out_proj, chained by programmatic dependent launch.
+// One decode step (T = 1): in_proj (weights as the 128-row operand, raw fp32 projections) -> gates, conv +
+// conv-state roll + gated delta rule + gated RMSNorm (decode_step_kernel, which loads the state and the
+// conv history while the GEMM runs) -> out_proj, chained by programmatic dependent launch.
 // proj [B, proj_ld] fp32 and y [B, vd] bf16 are scratch.
 // q8: with fp8 weights, the workspace region for the e4m3 activations and their scales (q8_bytes); the
 // projections then run as quantize_rows_fp8 + gemm_f8_tn.
@@ -530,11 +530,6 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   ep.a_tiled = L->w_in;
   ep.out = proj;
   ep.ld = L->proj_ld;
-  ep.conv_rows = L->conv_dim;
-  ep.z_rows = L->vd;
-  ep.nheads = L->hv;
-  ep.a_log = L->a_log;
-  ep.dt_bias = L->dt_bias;
   uint8_t* xq = static_cast<uint8_t*>(q8);
   float* xs = q8 ? reinterpret_cast<float*>(xq + align256(static_cast<size_t>(B) * h)) : nullptr;
   uint8_t* yq = q8 ? reinterpret_cast<uint8_t*>(xs) + align256(static_cast<size_t>(B) * 4) : nullptr;
@@ -545,13 +540,13 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
     ep.a_tiled = L->w_in8;
     ep.row_scale = L->s_in;
     ep.col_scale = xs;
-    GDN_CUDA(gemm_f8_tn(L->w_in8, xq, h, L->rows, B, h, kEpiDecodeInProj, ep, stream, true, true));
+    GDN_CUDA(gemm_f8_tn(L->w_in8, xq, h, L->rows, B, h, kEpiStoreF32T, ep, stream, true, true));
   } else if (w8) {
     ep.a_tiled = L->w_in8;
     ep.row_scale = L->s_in;
-    GDN_CUDA(gemm_w8_tn(L->w_in8, x, h, L->rows, B, h, kEpiDecodeInProj, ep, stream, true, true));
+    GDN_CUDA(gemm_w8_tn(L->w_in8, x, h, L->rows, B, h, kEpiStoreF32T, ep, stream, true, true));
   } else {
-    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiDecodeInProj, ep, 0, stream, true, true));
+    GDN_CUDA(gemm_bf16_tn(L->w_in, h, x, h, L->rows, B, h, kEpiStoreF32T, ep, 0, stream, true, true));
   }
   if (marks) {
     GDN_CUDA(stage_mark(L, 1, stream));
@@ -565,6 +560,8 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   ra.z = proj + z_off; ra.z_tok = L->proj_ld; ra.z_head = kHeadDim;
   ra.g = proj + a_off; ra.g_tok = L->proj_ld; ra.g_head = 1;
   ra.beta = proj + b_off; ra.b_tok = L->proj_ld; ra.b_head = 1;
+  ra.a_log = L->a_log;
+  ra.dt_bias = L->dt_bias;
   ra.norm_w = L->norm_w;
   ra.eps = L->dims.eps;
   ra.y = y; ra.y_tok = L->vd; ra.y_head = kHeadDim;

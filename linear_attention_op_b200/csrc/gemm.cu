@@ -113,26 +113,6 @@ __device__ __forceinline__ void epilogue16(const GemmEpiArgs& ep, int m, int n0,
       for (int j = 0; j < 16; ++j)
         if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = __float2bfloat16_rn(v[j]);
     }
-  } else {  // kEpiDecodeInProj
-    float* out = static_cast<float*>(ep.out);
-    const int cr = ep.conv_rows;
-    if (m < cr + ep.z_rows) {  // conv rows (raw: the conv runs in the decode step kernel) and z rows
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = v[j];
-    } else if (m < cr + ep.z_rows + ep.nheads) {
-      // g = -exp(A_log) * softplus(a + dt_bias)   (9B/kernels/layer_compute.cpp:160-166)
-      const int h = m - cr - ep.z_rows;
-      const float neg_a = -expf(ep.a_log[h]), dtb = ep.dt_bias[h];
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = neg_a * softplus_f(v[j] + dtb);
-    } else {
-      // beta = sigmoid(b)   (layer_compute.cpp:176-177)
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (n0 + j < N) out[static_cast<int64_t>(n0 + j) * ep.ld + m] = sigmoid_f(v[j]);
-    }
   }
 }
 
@@ -210,8 +190,7 @@ __device__ __forceinline__ void gemm_tn_body(const CUtensorMap& tmA, const CUten
   if (warp == 0) {
     if (elect_one()) {
       // Decode (transposed epilogues): A is the weight matrix, streamed exactly once.
-      const bool a_streamed = EPI == kEpiStoreF32T || EPI == kEpiStoreBF16T || EPI == kEpiDecodeInProj ||
-                              EPI == kEpiSwiGLUT;
+      const bool a_streamed = EPI == kEpiStoreF32T || EPI == kEpiStoreBF16T || EPI == kEpiSwiGLUT;
       const uint64_t pol_a = a_streamed ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = policy_evict_last();
       // The weight operand (A for the transposed decode epilogues, B otherwise) does not depend on the
@@ -338,22 +317,30 @@ __device__ __forceinline__ void tn_epilogue(uint32_t tmem, uint8_t* smem, const 
       const uint32_t part_addr = smem_u32(smem);
 #pragma unroll 1
       for (int c0 = split * 16; c0 < BN; c0 += 16 * ksplit) {
+        // every slice's 16 columns are requested before the first is summed: one distributed-shared-memory
+        // round trip per chunk instead of one per slice; the sum still runs in slice order
+        float4 p4[8][4];
+#pragma unroll
+        for (int rank = 0; rank < 8; ++rank) {
+          if (rank < ksplit) {
+            const uint32_t base = mapa_shared(part_addr, rank);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              p4[rank][i] = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
+          }
+        }
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
 #pragma unroll
         for (int rank = 0; rank < 8; ++rank) {
           if (rank < ksplit) {
-            const uint32_t base = mapa_shared(part_addr, rank);
-            float4 p4[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) p4[i] = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              v[4 * i] += p4[i].x;
-              v[4 * i + 1] += p4[i].y;
-              v[4 * i + 2] += p4[i].z;
-              v[4 * i + 3] += p4[i].w;
+              v[4 * i] += p4[rank][i].x;
+              v[4 * i + 1] += p4[rank][i].y;
+              v[4 * i + 2] += p4[rank][i].z;
+              v[4 * i + 3] += p4[rank][i].w;
             }
           }
         }
@@ -527,7 +514,6 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMa
     case kEpiStoreBF16: return launch_gemm<BN, STAGES, kEpiStoreBF16>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     case kEpiStoreF32T: return launch_gemm<BN, STAGES, kEpiStoreF32T>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
-    case kEpiDecodeInProj: return launch_gemm<BN, STAGES, kEpiDecodeInProj>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     case kEpiSwiGLUT: return launch_gemm<BN, STAGES, kEpiSwiGLUT>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     default: return cudaErrorInvalidValue;
   }
@@ -647,8 +633,8 @@ static cudaError_t dispatch_epi_f8(int epi, const CUtensorMap& ta, const CUtenso
                                    int ksplit, const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t s) {
   switch (epi) {
     case kEpiStoreBF16T: return launch_gemm<BN, STAGES, kEpiStoreBF16T, true>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
-    case kEpiDecodeInProj:
-      return launch_gemm<BN, STAGES, kEpiDecodeInProj, true>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
+    case kEpiStoreF32T:
+      return launch_gemm<BN, STAGES, kEpiStoreF32T, true>(ta, tb, M, N, K, ksplit, ep, pdl, trigger, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -915,8 +901,8 @@ static cudaError_t dispatch_w8(int epi, const CUtensorMap& tb, const void* a8, i
                                const GemmEpiArgs& ep, bool pdl, bool trigger, cudaStream_t s, int sms) {
   switch (epi) {
     case kEpiStoreBF16T: return launch_w8<BN, STAGES, NCONV, kEpiStoreBF16T>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
-    case kEpiDecodeInProj:
-      return launch_w8<BN, STAGES, NCONV, kEpiDecodeInProj>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
+    case kEpiStoreF32T:
+      return launch_w8<BN, STAGES, NCONV, kEpiStoreF32T>(tb, a8, M, N, K, ep, pdl, trigger, s, sms);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -12,10 +12,6 @@ enum GemmEpi : int {
   kEpiStoreBF16 = 1,     // out[m * ld + n] = bf16(acc)
   kEpiStoreF32T = 2,     // out[n * ld + m] = acc          (A = weights, B = activations)
   kEpiStoreBF16T = 3,    // out[n * ld + m] = bf16(acc)
-  kEpiDecodeInProj = 4,  // transposed store of the fused in_proj of one decode token per sequence:
-                         //   rows [0, conv_rows + z_rows): plain (the conv runs in the decode step kernel)
-                         //   next nheads rows: g = -exp(A_log) softplus(a + dt_bias)
-                         //   next nheads rows: beta = sigmoid(b)
   kEpiPrefillInProj = 5, // row-major fp32 store of the prefill in_proj (rows = tokens of seq_len-token
                          // sequences); columns [0, conv_rows) get the causal conv (K = 4) + SiLU, the
                          // raw last 3 inputs of each sequence go to conv_tail (persistent kernel only)
@@ -28,13 +24,8 @@ enum GemmEpi : int {
 struct GemmEpiArgs {
   void* out = nullptr;
   int64_t ld = 0;  // leading dimension of `out`, in elements
-  // kEpiDecodeInProj and kEpiPrefillInProj
+  // kEpiPrefillInProj
   int conv_rows = 0;
-  // kEpiDecodeInProj only
-  int z_rows = 0;
-  int nheads = 0;
-  const float* a_log = nullptr;   // [nheads]
-  const float* dt_bias = nullptr; // [nheads]
   // kEpiPrefillInProj only
   const float* conv_w = nullptr;  // [conv_rows, 4]
   const float* conv_state = nullptr;  // [M / seq_len, 3, conv_rows], read (the roll runs after the GEMM)
@@ -101,7 +92,7 @@ cudaError_t tile_weights_bf16(const void* src, int64_t ld, int rows, int cols, v
 //     xq [rows, cols] bytes and xs[rows]; launched with programmatic dependent launch.
 //   gemm_f8_tn: gemm_bf16_tn's weight-streaming path with A = w8 (pre-tiled e4m3, ep.a_tiled == A) and
 //     B = xq [N, K] (row stride ldb bytes), ep.row_scale / ep.col_scale set; epi kEpiStoreBF16T or
-//     kEpiDecodeInProj.
+//     kEpiStoreF32T.
 //   row_amax (optional): use these row maxima instead of the tiled rows' own (the rows of a column shard
 //     then get the scales of the whole rows, so every shard quantises as the unsharded matrix does).
 cudaError_t quantize_tiled_weights_fp8(void* w_tiled, int rows, int cols, void* w8, float* scale,
@@ -115,7 +106,7 @@ cudaError_t gemm_f8_tn(const void* A_tiled, const void* B, int64_t ldb, int M, i
 // Weight-only fp8: A8_tiled = e4m3 weights in the fp8 streaming layout (quantize_tiled_weights_fp8), B = bf16
 // activations [N, K] (row stride ldb elements), K % 128 == 0, ep.row_scale = the weights' row scales and
 // ep.col_scale null; the e4m3 stages are widened to bf16 in shared memory and multiplied on the bf16 tensor
-// cores.  epi kEpiStoreBF16T (optionally with ep.residual) or kEpiDecodeInProj.
+// cores.  epi kEpiStoreBF16T (optionally with ep.residual) or kEpiStoreF32T.
 cudaError_t gemm_w8_tn(const void* A8_tiled, const void* B, int64_t ldb, int M, int N, int K, int epi,
                        const GemmEpiArgs& args, cudaStream_t stream, bool pdl = false, bool trigger = false);
 

@@ -21,6 +21,10 @@ struct RecurrenceArgs {
   int64_t g_tok = 0, g_head = 0;
   const float* beta = nullptr;
   int64_t b_tok = 0, b_head = 0;
+  // Layer decode only: when a_log is set, g and beta above point at the raw a and b projections, and
+  // g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) are formed in the kernel.
+  const float* a_log = nullptr;    // [Hv]
+  const float* dt_bias = nullptr;  // [Hv]
   // Gated RMSNorm epilogue (when z != nullptr): y = RMSNorm(o) * norm_w * SiLU(z) -> bf16
   const float* z = nullptr;
   int64_t z_tok = 0, z_head = 0;

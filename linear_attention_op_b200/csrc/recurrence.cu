@@ -222,8 +222,15 @@ __global__ void __launch_bounds__(kRecThreads, 2) decode_step_kernel(RecurrenceA
   if (tid >= kHeadDim) {  // threads 128..255 have one conv channel, 0..127 two
     s_z[tid - kHeadDim] = a.z[row * a.z_tok + h * a.z_head + tid - kHeadDim];
     if (tid == kHeadDim) {
-      s_scal[0] = expf(a.g[row * a.g_tok + h * a.g_head]);
-      s_scal[1] = a.beta[row * a.b_tok + h * a.b_head];
+      const float ga = a.g[row * a.g_tok + h * a.g_head], gb = a.beta[row * a.b_tok + h * a.b_head];
+      if (a.a_log) {  // raw projections: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+        // (9B/kernels/layer_compute.cpp:160-166,176-177)
+        s_scal[0] = expf(-expf(a.a_log[h]) * softplus_f(ga + a.dt_bias[h]));
+        s_scal[1] = sigmoid_f(gb);
+      } else {
+        s_scal[0] = expf(ga);
+        s_scal[1] = gb;
+      }
     }
   }
   cp_async_wait_all();              // each thread reads back only the history it copied
