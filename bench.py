@@ -394,6 +394,8 @@ def run_ours(args):
         end.record(stream)
         torch.cuda.synchronize()
     barrier(world)
+    if max_over_ranks(float(device_error()), world) != 0:  # e.g. a peer wait that ran out: no number
+        raise SystemExit("device error during the timed decode steps")
     ms = max_over_ranks(start.elapsed_time(end), world)
     ms_step = ms / args.steps
     value = B * args.steps / (ms / 1e3)

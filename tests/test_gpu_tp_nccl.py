@@ -45,6 +45,12 @@ def _worker(rank, world, port, q):
         s_loc = layer.get_recurrent_state()
         yd = layer(xd)
         s_loc_d = layer.get_recurrent_state()
+        # several decode calls in a row: the NVLink all-reduce's slots, epoch and push counters cycle
+        xs = O.make_hidden(2, 5, 1024, seed=10)
+        want_s, s_want_s, _ = O.layer_forward(w, xs, s_want_d, O.layer_forward(w, xd, s_want, c_want,
+                                                                              mode="recurrent")[2], mode="recurrent")
+        ys = torch.cat([layer(xs[:, t:t + 1]) for t in range(5)], 1)
+        s_loc_s = layer.get_recurrent_state()
         # an output above the NVLink all-reduce's 8 MiB slot (4104 x 1024 bf16) takes the NCCL path
         xl = O.make_hidden(1, 4104, 1024, seed=9)
         yl = Qwen35GatedDeltaNet(weights=w, batch=1, tp_rank=rank, tp_size=world, comm=comm)(xl)
@@ -82,7 +88,9 @@ def _worker(rank, world, port, q):
             state_dec=O.max_abs_rel(s_loc_d, s_want_d[:, rank * hv:(rank + 1) * hv]), err=err,
             out_fp8=O.max_abs_rel(yq.float(), want_q), dec_pre=O.max_abs_rel(ydp.float(), want_dp),
             dec_dec=O.max_abs_rel(ydd.float(), want_dd),
-            dec_state=O.max_abs_rel(dec.get_recurrent_state(), sd[:, rank * hv:(rank + 1) * hv]))
+            dec_state=O.max_abs_rel(dec.get_recurrent_state(), sd[:, rank * hv:(rank + 1) * hv]),
+            out_steps=O.max_abs_rel(ys.float(), want_s),
+            state_steps=O.max_abs_rel(s_loc_s, s_want_s[:, rank * hv:(rank + 1) * hv]))
         if rank == 0:
             res["out_large"] = O.max_abs_rel(yl.float(), O.layer_forward(w, xl, mode="chunk")[0])
         comm.close()
@@ -114,7 +122,8 @@ def test_tensor_parallel_layer_nccl(world):
         assert "exc" not in r, r.get("exc")
         print(rank, r)
         assert r["err"] == 0
-        assert r["out"] <= 2e-2 and r["out_dec"] <= 2e-2, r
+        assert r["out"] <= 2e-2 and r["out_dec"] <= 2e-2 and r["out_steps"] <= 2e-2, r
+        assert r["state_steps"] <= 1e-3, r
         assert r["state"] <= 1e-3 and r["state_dec"] <= 1e-3, r
         assert r["out_fp8"] <= 2e-2, r
         assert r["dec_pre"] <= 2e-2 and r["dec_dec"] <= 2e-2 and r["dec_state"] <= 1e-3, r
