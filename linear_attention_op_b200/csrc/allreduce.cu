@@ -53,30 +53,21 @@ __device__ __forceinline__ bool wait_flag(const unsigned long long* p, unsigned 
   }
 }
 
-// Thread 0 waits for flags[0 .. world) >= e of this rank's page; the CTA learns the outcome.
-__device__ __forceinline__ bool cta_wait_all(const unsigned long long* flags, int world, unsigned long long e,
-                                             int* s_abort) {
-  if (threadIdx.x == 0)
-    for (int p = 0; p < world; ++p)
-      if (!wait_flag(flags + p, e)) {
-        *s_abort = 1;
-        break;
-      }
+// Lane p of warp 0 waits for flags[p * stride] >= e, p in [0, world), all flags polled at once (an acquire
+// load at system scope costs an L2 round trip, so world sequential polls would cost world of them); the CTA
+// learns the outcome.
+__device__ __forceinline__ bool cta_wait_all_stride(const unsigned long long* flags, int stride, int world,
+                                                    unsigned long long e, int* s_abort) {
+  if (threadIdx.x < 32) {
+    const bool ok = threadIdx.x >= world || wait_flag(flags + static_cast<int64_t>(threadIdx.x) * stride, e);
+    if (!__all_sync(0xffffffffu, ok) && threadIdx.x == 0) *s_abort = 1;
+  }
   __syncthreads();
   return *s_abort == 0;
 }
-
-// Thread 0 waits for flags[p * stride] >= e for p in [0, world); the CTA learns the outcome.
-__device__ __forceinline__ bool cta_wait_all_stride(const unsigned long long* flags, int stride, int world,
-                                                    unsigned long long e, int* s_abort) {
-  if (threadIdx.x == 0)
-    for (int p = 0; p < world; ++p)
-      if (!wait_flag(flags + static_cast<int64_t>(p) * stride, e)) {
-        *s_abort = 1;
-        break;
-      }
-  __syncthreads();
-  return *s_abort == 0;
+__device__ __forceinline__ bool cta_wait_all(const unsigned long long* flags, int world, unsigned long long e,
+                                             int* s_abort) {
+  return cta_wait_all_stride(flags, 1, world, e, s_abort);
 }
 
 // Sum of the world partials of 8 bf16 (vector i of each slot), in rank order.

@@ -556,7 +556,10 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
       // Wide batches (tensor-parallel decode: 64 sequences per GPU, so 128 .. 512 token columns): every CTA
       // streams its K range of one weight tile and of BN token rows, so per-CTA bytes ~ K / ksplit * (128 +
       // BN).  Wider token tiles mean fewer tiles, hence a deeper split inside one wave, hence fewer bytes per
-      // CTA: pick the BN in {64, 128, 256} that minimises them (64 keeps its two-CTAs-per-SM path).
+      // CTA; but a split's fp32 partial tile (128 x BN x 4 bytes, (ksplit - 1) / ksplit of it crossing to
+      // other CTAs) is reduced through distributed shared memory, which measured about 8 times slower per
+      // byte than streaming operands: pick the BN in {64, 128, 256} that minimises the sum (64 keeps its
+      // two-CTAs-per-SM path).
       const int m_tiles = (M + kBM - 1) / kBM, kblocks = (K + kBK - 1) / kBK;
       int best_bn = 64;
       double best = 1e30;
@@ -566,7 +569,8 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
         if (bn == 64) ks = t > sms ? std::max(1, std::min(8, 2 * sms / t)) : std::max(1, std::min(8, sms / t));
         else if (t <= sms) ks = std::max(1, std::min(8, sms / t));
         else continue;
-        const double cost = static_cast<double>((kblocks + ks - 1) / ks) * (kBM + bn);
+        const double cost = static_cast<double>((kblocks + ks - 1) / ks) * (kBM + bn) +
+                            8.0 * 4.0 * bn * (ks - 1) / ks;  // operand rows of 128 B + the reduction, as rows
         if (cost < best - 1e-9) {
           best = cost;
           best_bn = bn;
