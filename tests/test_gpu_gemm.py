@@ -51,6 +51,21 @@ def test_gemm_split_k_cluster(ksplit):
     assert err < 1e-4, err
 
 
+@pytest.mark.parametrize("tokens", [128, 256])
+@pytest.mark.parametrize("ksplit", [2, 3, 5])
+def test_gemm_split_k_wide_tiles(tokens, ksplit):
+    """128- and 256-token tiles split over 2, 3 and 5 CTAs: chunks owned round-robin, more than one per CTA;
+    the result is the same for every split up to the reduction order."""
+    g = torch.Generator(device="cuda").manual_seed(tokens + ksplit)
+    w = torch.randn(384, 1536, device="cuda", generator=g).bfloat16()
+    x = torch.randn(tokens, 1536, device="cuda", generator=g).bfloat16()
+    want = (w.float() @ x.float().T).T
+    got = run_gemm(w, x, 2, ksplit)
+    err = ((got - want).abs().max() / want.abs().max()).item()
+    assert err < 1e-4, err
+    assert torch.equal(got, run_gemm(w, x, 2, ksplit)), "split-K result not reproducible"
+
+
 def test_gemm_9b_decode_inproj_shape():
     g = torch.Generator(device="cuda").manual_seed(1)
     w = (torch.randn(12352, 4096, device="cuda", generator=g) * 0.02).bfloat16()
