@@ -576,9 +576,11 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
   ra.v_conv = 2 * L->kd;
   GDN_CUDA(decode_step_forward(ra, stream));
   if (marks) GDN_CUDA(stage_mark(L, 4, stream));
-  // out_proj lets its successor launch at once (the next step's in_proj, or the all-reduce): that kernel
-  // touches nothing but its weights before its own dependent wait, which returns only after out_proj (and
-  // so everything before it) has completed, and SMs left idle by out_proj's 128 CTAs start its weight ring.
+  // Without an all-reduce after it, out_proj lets its successor (the next step's in_proj) launch at once:
+  // that kernel touches nothing but its weights before its own dependent wait, which returns only after
+  // out_proj (and so everything before it) has completed, and SMs left idle by out_proj's CTAs start its
+  // weight ring.
+  const bool out_trigger = slot_epoch == nullptr;
   GemmEpiArgs eo;
   eo.out = out;
   eo.ld = h;
@@ -590,13 +592,13 @@ static gdn_status decode_chain(gdn_layer* L, const uint16_t* x, int B, float* re
     eo.a_tiled = L->w_out8;
     eo.row_scale = L->s_out;
     eo.col_scale = ys;
-    GDN_CUDA(gemm_f8_tn(L->w_out8, yq, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true, true));
+    GDN_CUDA(gemm_f8_tn(L->w_out8, yq, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true, out_trigger));
   } else if (w8) {
     eo.a_tiled = L->w_out8;
     eo.row_scale = L->s_out;
-    GDN_CUDA(gemm_w8_tn(L->w_out8, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true, true));
+    GDN_CUDA(gemm_w8_tn(L->w_out8, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, stream, true, out_trigger));
   } else {
-    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true, true));
+    GDN_CUDA(gemm_bf16_tn(L->w_out, L->vd, y, L->vd, h, B, L->vd, kEpiStoreBF16T, eo, 0, stream, true, out_trigger));
   }
   if (marks) GDN_CUDA(stage_mark(L, 5, stream));
   return GDN_OK;

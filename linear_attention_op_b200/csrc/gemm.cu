@@ -1362,6 +1362,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int r = q * 32 + lane;
     const int etid = (warp - 2) * 32 + lane;
     const bool issuer = etid == half * 128;  // one thread per half issues the TMA stores
+    const uint64_t out_policy = policy_evict_first();
     uint8_t* stage = smem + kPOutStage + half * kBM * 64;
     const float4* cw = reinterpret_cast<const float4*>(smem + kPConvW);
     float* xs = reinterpret_cast<float*>(smem + kPXch) + half * 4 * 48;
@@ -1446,7 +1447,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         fence_proxy_async_shared();
         epi_half_sync(half);
         if (issuer) {
-          tma_store_2d(&tmOut, stage, kSwiGLU ? n0 / 2 : n0, mt * m_stride);
+          // the output streams past L2 (evict-first) so that the x row blocks and weight tiles of the
+          // current raster group stay resident
+          tma_store_2d_hint(&tmOut, stage, kSwiGLU ? n0 / 2 : n0, mt * m_stride, out_policy);
           bulk_commit();
         }
       }

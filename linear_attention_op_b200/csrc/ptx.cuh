@@ -143,6 +143,15 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// The same store with an L2 cache policy (createpolicy), e.g. evict-first for an output that is not re-read
+// soon, so that it does not push operands the kernel keeps re-reading out of L2.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* src, int x, int y,
+                                                  uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                   map),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
