@@ -317,31 +317,23 @@ __device__ __forceinline__ void tn_epilogue(uint32_t tmem, uint8_t* smem, const 
       const uint32_t part_addr = smem_u32(smem);
 #pragma unroll 1
       for (int c0 = split * 16; c0 < BN; c0 += 16 * ksplit) {
-        // every slice's 16 columns are requested before the first is summed: one distributed-shared-memory
-        // round trip per chunk instead of one per slice; the sum still runs in slice order
-        float4 p4[8][4];
-#pragma unroll
-        for (int rank = 0; rank < 8; ++rank) {
-          if (rank < ksplit) {
-            const uint32_t base = mapa_shared(part_addr, rank);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              p4[rank][i] = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
-          }
-        }
+        // slice by slice, in slice order (holding every slice's columns at once took ~130 more registers
+        // per thread, 190 in all, which left the two-CTAs-per-SM launches one CTA per SM: two waves)
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
+#pragma unroll 1
+        for (int rank = 0; rank < ksplit; ++rank) {
+          const uint32_t base = mapa_shared(part_addr, rank);
+          float4 p4[4];
 #pragma unroll
-        for (int rank = 0; rank < 8; ++rank) {
-          if (rank < ksplit) {
+          for (int i = 0; i < 4; ++i) p4[i] = ld_dsmem_f4(base + static_cast<uint32_t>(((c0 / 4 + i) * kBM + r) * 16));
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              v[4 * i] += p4[rank][i].x;
-              v[4 * i + 1] += p4[rank][i].y;
-              v[4 * i + 2] += p4[rank][i].z;
-              v[4 * i + 3] += p4[rank][i].w;
-            }
+          for (int i = 0; i < 4; ++i) {
+            v[4 * i] += p4[i].x;
+            v[4 * i + 1] += p4[i].y;
+            v[4 * i + 2] += p4[i].z;
+            v[4 * i + 3] += p4[i].w;
           }
         }
         apply_scales(eo, m, n_tile * BN + c0, M, N, v);
