@@ -550,19 +550,25 @@ cudaError_t gemm_bf16_tn(const void* A, int64_t lda, const void* B, int64_t ldb,
       // BN).  Wider token tiles mean fewer tiles, hence a deeper split inside one wave, hence fewer bytes per
       // CTA; but a split's fp32 partial tile (128 x BN x 4 bytes, (ksplit - 1) / ksplit of it crossing to
       // other CTAs) is reduced through distributed shared memory, which measured about 8 times slower per
-      // byte than streaming operands: pick the BN in {64, 128, 256} that minimises the sum (64 keeps its
-      // two-CTAs-per-SM path).
+      // byte than streaming operands.  Pick the BN in {64, 128, 256} that minimises the sum per SM (64 keeps
+      // its two-CTAs-per-SM path for more tiles than SMs, where the two CTAs share the SM: at 128 tokens and
+      // one GPU, 194 such tiles ran a layer step in 159 us, 97 tiles of 128 tokens in 135 us).
       const int m_tiles = (M + kBM - 1) / kBM, kblocks = (K + kBK - 1) / kBK;
       int best_bn = 64;
       double best = 1e30;
       for (int bn : {64, 128, 256}) {
         const int t = m_tiles * ((N + bn - 1) / bn);
-        int ks;
-        if (bn == 64) ks = t > sms ? std::max(1, std::min(8, 2 * sms / t)) : std::max(1, std::min(8, sms / t));
-        else if (t <= sms) ks = std::max(1, std::min(8, sms / t));
-        else continue;
-        const double cost = static_cast<double>((kblocks + ks - 1) / ks) * (kBM + bn) +
-                            8.0 * 4.0 * bn * (ks - 1) / ks;  // operand rows of 128 B + the reduction, as rows
+        int ks, per_sm = 1;  // CTAs sharing an SM's bandwidth
+        if (bn == 64 && t > sms) {
+          ks = std::max(1, std::min(8, 2 * sms / t));
+          per_sm = 2;
+        } else if (bn == 64 || t <= sms) {
+          ks = std::max(1, std::min(8, sms / t));
+        } else {
+          continue;
+        }
+        const double cost = per_sm * (static_cast<double>((kblocks + ks - 1) / ks) * (kBM + bn) +
+                                      8.0 * 4.0 * bn * (ks - 1) / ks);  // operand rows of 128 B + the reduction
         if (cost < best - 1e-9) {
           best = cost;
           best_bn = bn;
