@@ -423,10 +423,14 @@ def run_ours(args):
     # End to end through the public API with pinned host buffers: every step copies its input host->device
     # and its result device->host inside the timed region (forward_host_async: the copies run on copy streams
     # with double-buffered device rows, overlapping the neighbouring steps' compute).
+    # With several GPUs the ranks share the host traffic (split_io): rank r copies its 1/N of the sequences in
+    # and out, and the communicator all-gathers the input over NVLink, so the job moves each step's input and
+    # result across PCIe once instead of N times.
     xh = x.detach().cpu().pin_memory()
     yh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
+    split = world > 1
     for i in range(3):
-        layer.forward_host_async(xh, yh[i % 2])
+        layer.forward_host_async(xh, yh[i % 2], split_io=split)
     torch.cuda.synchronize()
     barrier(world)
     e2e_steps = max(args.steps, 20)
@@ -435,7 +439,7 @@ def run_ours(args):
     t0 = time.perf_counter()
     es.record()
     for i in range(e2e_steps):
-        ev = layer.forward_host_async(xh, yh[i % 2])
+        ev = layer.forward_host_async(xh, yh[i % 2], split_io=split)
     ev.synchronize()
     ee.record()
     torch.cuda.synchronize()
@@ -444,7 +448,9 @@ def run_ours(args):
            "h2d_bytes_per_step": xh.numel() * xh.element_size(),
            "d2h_bytes_per_step": yh[0].numel() * yh[0].element_size(), "steps": e2e_steps,
            "path": "Qwen35GatedDeltaNet.forward_host_async (C-ABI gdn_layer_forward), pinned host in/out, "
-                   "copies on copy streams overlapping the neighbouring steps",
+                   "copies on copy streams overlapping the neighbouring steps" +
+                   (f"; split_io: each of the {world} ranks copies 1/{world} of the sequences in and out and "
+                    "all-gathers the input over NVLink (bytes above = the whole job's)" if split else ""),
            "timing": "max of host wall clock and CUDA events around all steps, max over ranks"}
 
     result = {

@@ -238,6 +238,10 @@ GDN_API gdn_status gdn_gemm_bf16(const uint16_t* a, int64_t lda, const uint16_t*
 GDN_API gdn_status gdn_comm_get_unique_id(void* id_out, size_t id_bytes);
 GDN_API gdn_status gdn_comm_create(const void* id, size_t id_bytes, int32_t rank, int32_t world, gdn_comm** out_comm);
 GDN_API gdn_status gdn_comm_destroy(gdn_comm* comm);
+/* In-place all-gather over the communicator on `stream`: rank r's bytes_per_rank bytes at
+ * buf + r * bytes_per_rank are copied to the same offset on every rank (ncclAllGather).  Used to give every
+ * rank of a tensor-parallel layer the whole input when each rank copied only its share from the host. */
+GDN_API gdn_status gdn_comm_allgather(gdn_comm* comm, void* buf, size_t bytes_per_rank, void* stream);
 
 /* Synchronises the current device and returns (and clears) the device error word that bounded waits
  * inside the kernels set; 0 = no error.  After a peer-wait code (0x105: an NVLink all-reduce gave up

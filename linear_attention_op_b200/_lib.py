@@ -21,7 +21,7 @@ STATUS_NAMES = {
 # Every symbol the header declares (checked by tests/test_abi_exports.py).
 EXPORTED = (
     "gdn_layer_create", "gdn_layer_destroy", "gdn_layer_get_info", "gdn_layer_reserve", "gdn_layer_forward",
-    "gdn_recurrence_forward", "gdn_comm_get_unique_id", "gdn_comm_create", "gdn_comm_destroy",
+    "gdn_recurrence_forward", "gdn_comm_get_unique_id", "gdn_comm_create", "gdn_comm_destroy", "gdn_comm_allgather",
     "gdn_device_error", "gdn_last_error_string", "gdn_kernel_launch_count", "gdn_abi_version", "gdn_gemm_bf16",
     "gdn_layer_set_stage_events", "gdn_layer_decode_static", "gdn_layer_share_workspace",
     "gdn_layer_set_weight_format", "gdn_selftest_peer_wait", "gdn_layer_reserve_batch", "gdn_layer_set_max_rows",
@@ -82,6 +82,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gdn_comm_get_unique_id": [P, ctypes.c_size_t],
         "gdn_comm_create": [P, ctypes.c_size_t, I32, I32, ctypes.POINTER(P)],
         "gdn_comm_destroy": [P],
+        "gdn_comm_allgather": [P, P, ctypes.c_size_t, P],
         "gdn_device_error": [ctypes.POINTER(I32)],
         "gdn_gemm_bf16": [P, I64, P, I64, I32, I32, I32, I32, P, I64, I32, P],
         "gdn_layer_set_stage_events": [P, ctypes.POINTER(P), I32],

@@ -1125,6 +1125,19 @@ extern "C" gdn_status gdn_comm_destroy(gdn_comm* c) {
   return GDN_OK;
 }
 
+extern "C" gdn_status gdn_comm_allgather(gdn_comm* c, void* buf, size_t bytes_per_rank, void* stream) {
+  if (!c || !buf) return fail(GDN_ERR_NULL_POINTER, "gdn_comm_allgather: null argument");
+  if (bytes_per_rank == 0) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_comm_allgather: zero bytes");
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(GDN_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  char* b = static_cast<char*>(buf);
+  // in place: this rank's share already sits at its offset
+  ncclResult_t r = api.allGather(b + static_cast<size_t>(c->rank) * bytes_per_rank, b, bytes_per_rank, ncclChar,
+                                 c->comm, static_cast<cudaStream_t>(stream));
+  if (r != ncclSuccess) return fail(GDN_ERR_NCCL, "ncclAllGather: %s", api.getErrorString(r));
+  return GDN_OK;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Misc
 // ------------------------------------------------------------------------------------------------

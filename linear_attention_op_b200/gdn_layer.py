@@ -180,6 +180,7 @@ class Qwen35GatedDeltaNet:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.batch = batch
         self.comm = comm
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         w = LayerWeights.from_any(hf_layer if hf_layer is not None else weights)
         with torch.cuda.device(self.device):
             self._h = _LayerHandle(w, tp_rank, tp_size)
@@ -251,14 +252,24 @@ class Qwen35GatedDeltaNet:
             self.forward_into(x, out)
             return _to_caller(out, hidden_states, pinned)
 
-    def forward_host_async(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.cuda.Event:
+    def forward_host_async(self, x_host: torch.Tensor, out_host: torch.Tensor,
+                           split_io: bool = False) -> torch.cuda.Event:
         """Pinned host bf16 x [B, T, hidden] -> pinned host bf16 out, without waiting: the host-to-device copy,
         the layer call and the device-to-host copy are queued and the returned event completes when out_host
         holds the result.  Copies run on two copy streams with double-buffered device rows, so a call's
         input copy overlaps the previous call's compute and its result copy the next call's compute (the
         calls themselves stay in order on the current stream).  x_host must not change, and out_host must
-        not be read, before the event completes."""
+        not be read, before the event completes.
+
+        split_io (tensor-parallel layer with its communicator, batch divisible by the group size): the
+        ranks share the host traffic instead of each moving the whole batch -- rank r copies only sequences
+        [r B / G, (r + 1) B / G) of x_host in, the communicator all-gathers the other ranks' sequences over
+        NVLink before the call, and only rank r's sequences of the (identical) result are copied out to
+        out_host.  Every rank passes the whole input; the whole output is the union of the ranks' shares."""
         B, T, H = x_host.shape
+        G, r = self.tp_size, self.tp_rank
+        if split_io and (G == 1 or self.comm is None or B % G):
+            raise ValueError("split_io needs a tensor-parallel layer with its communicator and batch % tp_size == 0")
         if B != self.batch or H != self.hidden or tuple(out_host.shape) != (B, T, H):
             raise ValueError(f"x {tuple(x_host.shape)} / out {tuple(out_host.shape)} do not match [{self.batch}, T, {self.hidden}]")
         if x_host.dtype != torch.bfloat16 or out_host.dtype != torch.bfloat16 or not (x_host.is_pinned() and out_host.is_pinned()):
@@ -275,17 +286,20 @@ class Qwen35GatedDeltaNet:
             io["i"] = i ^ 1
             cur = torch.cuda.current_stream()
             hs, ds = io["h2d_stream"], io["d2h_stream"]
+            rows = slice(r * (B // G), (r + 1) * (B // G)) if split_io else slice(0, B)
             hs.wait_event(io["done"][i])  # the call that last read xin[i] has finished
             with torch.cuda.stream(hs):
-                io["xin"][i].copy_(x_host, non_blocking=True)
+                io["xin"][i][rows].copy_(x_host[rows], non_blocking=True)
                 io["h2d"][i].record(hs)
             cur.wait_event(io["h2d"][i])
             cur.wait_event(io["d2h"][i])  # the copy that last read xout[i] has finished
+            if split_io:
+                self.comm.allgather_(io["xin"][i], stream=cur)
             self.forward_into(io["xin"][i], io["xout"][i], stream=cur)
             io["done"][i].record(cur)
             ds.wait_event(io["done"][i])
             with torch.cuda.stream(ds):
-                out_host.copy_(io["xout"][i], non_blocking=True)
+                out_host[rows].copy_(io["xout"][i][rows], non_blocking=True)
                 io["d2h"][i].record(ds)
             return io["d2h"][i]
 

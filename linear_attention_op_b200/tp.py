@@ -83,6 +83,18 @@ class Communicator:
         dist.broadcast_object_list(obj, src=0, group=group)
         return cls(obj[0], rank, world)
 
+    def allgather_(self, buf, stream=None):
+        """In place over the group (gdn_comm_allgather): buf (contiguous, on this rank's device) is split into
+        world equal parts along its bytes; part r comes from rank r."""
+        import torch
+
+        if not buf.is_contiguous() or (buf.numel() * buf.element_size()) % self.world:
+            raise ValueError("allgather_ wants a contiguous buffer whose bytes divide by the world size")
+        s = stream if stream is not None else torch.cuda.current_stream(buf.device)
+        _lib.call("gdn_comm_allgather", self.handle, ctypes.c_void_p(buf.data_ptr()),
+                  buf.numel() * buf.element_size() // self.world, ctypes.c_void_p(s.cuda_stream))
+        return buf
+
     def close(self) -> None:
         if getattr(self, "handle", None) is not None and self.handle.value:
             _lib.lib().gdn_comm_destroy(self.handle)

@@ -51,6 +51,19 @@ def _worker(rank, world, port, q):
                                                                               mode="recurrent")[2], mode="recurrent")
         ys = torch.cat([layer(xs[:, t:t + 1]) for t in range(5)], 1)
         s_loc_s = layer.get_recurrent_state()
+        # the pipelined host path with the ranks sharing the host copies (split_io): rank r's sequences of
+        # the result equal forward_into's (8 sequences, so every group size divides the batch)
+        x8 = O.make_hidden(8, 2, 1024, seed=11).to(torch.bfloat16)
+        la = Qwen35GatedDeltaNet(weights=w, batch=8, tp_rank=rank, tp_size=world, comm=comm)
+        lb = Qwen35GatedDeltaNet(weights=w, batch=8, tp_rank=rank, tp_size=world, comm=comm)
+        rows = slice(rank * (8 // world), (rank + 1) * (8 // world))
+        split_same = True
+        for t in range(2):
+            xt = x8[:, t:t + 1].contiguous()
+            ya = la.forward_into(xt.cuda(), torch.empty(8, 1, 1024, dtype=torch.bfloat16, device="cuda")).cpu()
+            yb = torch.zeros(8, 1, 1024, dtype=torch.bfloat16).pin_memory()
+            lb.forward_host_async(xt.pin_memory(), yb, split_io=True).synchronize()
+            split_same = split_same and bool(torch.equal(yb[rows], ya[rows]))
         # an output above the NVLink all-reduce's 8 MiB slot (4104 x 1024 bf16) takes the NCCL path
         xl = O.make_hidden(1, 4104, 1024, seed=9)
         yl = Qwen35GatedDeltaNet(weights=w, batch=1, tp_rank=rank, tp_size=world, comm=comm)(xl)
@@ -89,7 +102,7 @@ def _worker(rank, world, port, q):
             out_fp8=O.max_abs_rel(yq.float(), want_q), dec_pre=O.max_abs_rel(ydp.float(), want_dp),
             dec_dec=O.max_abs_rel(ydd.float(), want_dd),
             dec_state=O.max_abs_rel(dec.get_recurrent_state(), sd[:, rank * hv:(rank + 1) * hv]),
-            out_steps=O.max_abs_rel(ys.float(), want_s),
+            out_steps=O.max_abs_rel(ys.float(), want_s), split_io_same=split_same,
             state_steps=O.max_abs_rel(s_loc_s, s_want_s[:, rank * hv:(rank + 1) * hv]))
         if rank == 0:
             res["out_large"] = O.max_abs_rel(yl.float(), O.layer_forward(w, xl, mode="chunk")[0])
@@ -124,6 +137,7 @@ def test_tensor_parallel_layer_nccl(world):
         assert r["err"] == 0
         assert r["out"] <= 2e-2 and r["out_dec"] <= 2e-2 and r["out_steps"] <= 2e-2, r
         assert r["state_steps"] <= 1e-3, r
+        assert r["split_io_same"], r
         assert r["state"] <= 1e-3 and r["state_dec"] <= 1e-3, r
         assert r["out_fp8"] <= 2e-2, r
         assert r["dec_pre"] <= 2e-2 and r["dec_dec"] <= 2e-2 and r["dec_state"] <= 1e-3, r
