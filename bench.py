@@ -423,12 +423,14 @@ def run_ours(args):
     # End to end through the public API with pinned host buffers: every step copies its input host->device
     # and its result device->host inside the timed region (forward_host_async: the copies run on copy streams
     # with double-buffered device rows, overlapping the neighbouring steps' compute).
-    # With several GPUs the ranks share the host traffic (split_io): rank r copies its 1/N of the sequences in
-    # and out, and the communicator all-gathers the input over NVLink, so the job moves each step's input and
-    # result across PCIe once instead of N times.
+    # With 4 or more GPUs the ranks share the host traffic (split_io): rank r copies its 1/N of the sequences
+    # in and out, and the communicator all-gathers the input over NVLink, so the job moves each step's input
+    # and result across PCIe once instead of N times (8 GPUs copying the whole batch each: 1.13 M tok/s, bound
+    # by the host side).  At 2 GPUs the all-gather on the call's stream costs more than it saves (1.11 against
+    # 1.28 M tok/s), so each rank copies the whole batch.
     xh = x.detach().cpu().pin_memory()
     yh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
-    split = world > 1
+    split = world >= 4
     for i in range(3):
         layer.forward_host_async(xh, yh[i % 2], split_io=split)
     torch.cuda.synchronize()
