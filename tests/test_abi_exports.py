@@ -114,4 +114,5 @@ def test_workspace_format_and_selftest_entry_points_check_pointers():
     assert lib.gdn_layer_decode_static(None, None, 1, None, None, None, None) == 2
     assert lib.gdn_layer_reserve_batch(None, 64, 1) == 2
     assert lib.gdn_layer_set_max_rows(None, 128) == 2
+    assert lib.gdn_comm_allgather(None, None, 16, None) == 2
     assert lib.gdn_last_error_string()
